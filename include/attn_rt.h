@@ -1,0 +1,176 @@
+/*
+ * attn_rt.h — C ABI of the B200 (sm_100a) runtime behind the `attention.fused` op.
+ *
+ * The reference project (luisroayerdi/MLIR-FlashAttention) defines one op,
+ *   attention.fused ins(%Q, %K, %V) scale(%s) [mask(%m)] outs(%O)
+ * (include/Attention/AttentionOps.td:20-54) and lowers it to a CPU loop nest
+ * (lib/Attention/TilingPass.cpp:155-392).  This library replaces that lowering:
+ * a pass rewrites the op into calls to the `_mlir_ciface_attn_fused_*` symbols
+ * below (MLIR's memref-descriptor C interface, the calling convention shown in
+ * the reference at examples/MatMUL/main.c:4-7,38-41), and every call ends in
+ * `attn_fwd`, which launches the hand-written sm_100a kernels.
+ *
+ * Semantics of one (batch, head) slice, identical to the reference op:
+ *   O = softmax(Q·Kᵀ·scale, masked entries -> -inf) · V
+ * The reference op is rank-2 f32 only; this ABI adds rank-4 [B,H,N,D] views,
+ * bf16 and fp8-e4m3 inputs (fp32 accumulation), grouped-query heads (Hq a
+ * multiple of Hkv), and an optional log-sum-exp output.
+ *
+ * Ownership and threading.  The caller owns every buffer; O (and LSE) are
+ * written in place, as the op's memory effects declare (AttentionOps.cpp:15-30).
+ * The runtime keeps only a per-device status word and, for host memrefs,
+ * per-device staging buffers, both created on first use behind a mutex.
+ * Calls on different streams may run concurrently.
+ *
+ * Errors.  Every entry point returns 0 on success or a negative ATTN_ERR_* code
+ * and never aborts.  `attn_rt_last_error()` returns the message of the last
+ * failure on the calling thread; shape errors reuse the reference verifier's
+ * wording (AttentionOps.cpp:39-56).
+ */
+#ifndef ATTN_RT_H
+#define ATTN_RT_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ATTN_API __attribute__((visibility("default")))
+#else
+#define ATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define ATTN_OK                 0
+#define ATTN_ERR_INVALID       -1  /* null descriptor or pointer                   */
+#define ATTN_ERR_SHAPE         -2  /* shapes inconsistent (verifier rules)         */
+#define ATTN_ERR_STRIDE        -3  /* head_dim not unit-stride or strides unusable */
+#define ATTN_ERR_DTYPE         -4  /* unsupported element type combination         */
+#define ATTN_ERR_ALIGN         -5  /* pointer/stride not 16-byte aligned           */
+#define ATTN_ERR_CUDA          -6  /* a CUDA runtime/driver call failed            */
+#define ATTN_ERR_TIMEOUT       -7  /* a bounded on-device wait expired             */
+#define ATTN_ERR_UNSUPPORTED   -8  /* valid op, variant not built (e.g. head_dim)  */
+#define ATTN_ERR_NO_DEVICE     -9  /* no sm_100 device visible                     */
+
+/* ---- element types and mask kinds --------------------------------------- */
+#define ATTN_F32   0
+#define ATTN_BF16  1
+#define ATTN_E4M3  2
+
+#define ATTN_MASK_NONE    0  /* no mask operand                                   */
+#define ATTN_MASK_CAUSAL  1  /* mask[i][j] = (j > i): the causal generic           */
+#define ATTN_MASK_DENSE   2  /* explicit i1 mask, one byte per element, 1 = masked */
+
+/*
+ * One attention call over B x Hq independent (batch, head) slices.
+ * Strides are in ELEMENTS for q/k/v/o ([0]=batch, [1]=head, [2]=row; the
+ * head_dim stride must be 1) and in BYTES for the dense mask.
+ * All data pointers are device pointers.
+ */
+typedef struct AttnDesc {
+  int32_t dtype;        /* ATTN_F32 / ATTN_BF16 / ATTN_E4M3: type of Q, K, V   */
+  int32_t out_dtype;    /* ATTN_F32 or ATTN_BF16: type of O                    */
+  int32_t mask_kind;    /* ATTN_MASK_*                                          */
+  int32_t flags;        /* reserved, must be 0                                  */
+  int64_t B, Hq, Hkv, Nq, Nk, D;
+  int64_t q_stride[3], k_stride[3], v_stride[3], o_stride[3];
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse;                /* optional [B,Hq,Nq] fp32 contiguous, natural log  */
+  const uint8_t* mask;       /* ATTN_MASK_DENSE only                             */
+  int64_t mask_stride[3];    /* bytes: batch, head, row; column stride is 1      */
+  float scale;               /* multiplies Q·Kᵀ (the op's `scale` operand)        */
+  float q_descale;           /* e4m3 only: dequantisation factors; else 1        */
+  float k_descale;
+  float v_descale;
+  int32_t* status;           /* optional device word for kernel status; if null
+                                the runtime's per-device word is used            */
+} AttnDesc;
+
+/* Asynchronous launch on `stream` (a cudaStream_t; NULL = legacy default).
+ * Replaces the loop nest TilingPass.cpp:188-386 emits for one attention.fused. */
+ATTN_API int attn_fwd(const AttnDesc* desc, void* stream);
+
+/* Select and initialise `device` (idempotent): checks for sm_100, creates the
+ * per-device status word.  Called implicitly by attn_fwd. */
+ATTN_API int attn_rt_init(int device);
+
+/* Synchronise `stream`, read and clear the device status word written by the
+ * kernels of `device`; returns ATTN_OK or the first recorded ATTN_ERR_*. */
+ATTN_API int attn_rt_check_status(int device, void* stream);
+
+/* Human-readable name of a status code. */
+ATTN_API const char* attn_rt_status_string(int code);
+
+/* Message of the last failure on the calling thread ("" if none). */
+ATTN_API const char* attn_rt_last_error(void);
+
+/* ABI version, (major << 16) | minor. */
+ATTN_API int attn_rt_version(void);
+
+/* Number of kernel launches attn_fwd issued in this process (all devices). */
+ATTN_API int64_t attn_rt_launch_count(void);
+
+/* ---- MLIR memref-descriptor interface ------------------------------------
+ * MLIR passes a memref<...> to an `llvm.emit_c_interface` function as a pointer
+ * to {allocated, aligned, offset, sizes[R], strides[R]} (strides in elements).
+ * The element type is fixed by the symbol name.  The buffers may be host or
+ * device memory: host buffers are staged through device memory in chunks of
+ * slices with copies overlapped with compute, and the call returns after O is
+ * back in host memory.  These calls are synchronous.
+ * Symbol naming: attn_fused_<dtype>_<variant>[_4d], variant in
+ * {nomask, causal, mask}; the lowering pass picks it from the mask operand.  */
+typedef struct AttnMemRef2D {
+  void* allocated;
+  void* aligned;
+  int64_t offset;
+  int64_t sizes[2];
+  int64_t strides[2];
+} AttnMemRef2D;
+
+typedef struct AttnMemRef4D {
+  void* allocated;
+  void* aligned;
+  int64_t offset;
+  int64_t sizes[4];
+  int64_t strides[4];
+} AttnMemRef4D;
+
+/* Rank-2 f32, the reference op's own form (AttentionOps.td:36-41). */
+ATTN_API int32_t _mlir_ciface_attn_fused_f32_nomask(AttnMemRef2D* Q, AttnMemRef2D* K, AttnMemRef2D* V,
+                                           float scale, AttnMemRef2D* O);
+ATTN_API int32_t _mlir_ciface_attn_fused_f32_causal(AttnMemRef2D* Q, AttnMemRef2D* K, AttnMemRef2D* V,
+                                           float scale, AttnMemRef2D* O);
+ATTN_API int32_t _mlir_ciface_attn_fused_f32_mask(AttnMemRef2D* Q, AttnMemRef2D* K, AttnMemRef2D* V,
+                                         float scale, AttnMemRef2D* mask, AttnMemRef2D* O);
+
+/* Rank-4 [B,H,N,D] f32 in / f32 out. */
+ATTN_API int32_t _mlir_ciface_attn_fused_f32_nomask_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
+                                              float scale, AttnMemRef4D* O);
+ATTN_API int32_t _mlir_ciface_attn_fused_f32_causal_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
+                                              float scale, AttnMemRef4D* O);
+
+/* Rank-4 bf16 in / bf16 out; LSE may be NULL or a memref<BxHxNqxf32> given as
+ * a 4-D descriptor whose last size is 1. */
+ATTN_API int32_t _mlir_ciface_attn_fused_bf16_nomask_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
+                                               float scale, AttnMemRef4D* O, AttnMemRef4D* LSE);
+ATTN_API int32_t _mlir_ciface_attn_fused_bf16_causal_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
+                                               float scale, AttnMemRef4D* O, AttnMemRef4D* LSE);
+
+/* Rank-4 e4m3 in (per-tensor dequantisation factors) / bf16 out. */
+ATTN_API int32_t _mlir_ciface_attn_fused_e4m3_nomask_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
+                                               float scale, float q_descale, float k_descale,
+                                               float v_descale, AttnMemRef4D* O, AttnMemRef4D* LSE);
+ATTN_API int32_t _mlir_ciface_attn_fused_e4m3_causal_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
+                                               float scale, float q_descale, float k_descale,
+                                               float v_descale, AttnMemRef4D* O, AttnMemRef4D* LSE);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ATTN_RT_H */

@@ -1,0 +1,130 @@
+// attn_fwd_f32.cuh — fp32 attention forward on the CUDA cores (sm_100a).
+//
+// The reference op is f32 end to end (include/Attention/AttentionOps.td:36-41)
+// and its users compare against it at 1e-4 relative tolerance, which TF32
+// tensor-core inputs (10-bit mantissa) cannot meet.  This kernel keeps every
+// product and sum in fp32 and follows the same online-softmax recurrence as
+// lib/Attention/TilingPass.cpp:279-374 (running max, alpha rescale, running
+// sum, final divide), with the general i1 mask operand supported
+// (TilingPass.cpp:254-277: masked -> -inf).
+//
+// Layout: CTA = 4 warps = 4 query rows of one (batch, head) slice; keys are
+// processed in chunks of 32 staged in shared memory (K with a padded row so
+// lane-per-key dot products are bank-conflict free, V unpadded for
+// lane-per-column accumulation).  Exponentials use expf.
+#pragma once
+
+#include <cstdint>
+
+namespace attn_f32 {
+
+struct F32Params {
+  const float* q;
+  const float* k;
+  const float* v;
+  float* o;
+  float* lse;
+  const uint8_t* mask;
+  int64_t q_sb, q_sh, q_sn;
+  int64_t k_sb, k_sh, k_sn;
+  int64_t v_sb, v_sh, v_sn;
+  int64_t o_sb, o_sh, o_sn;
+  int64_t m_sb, m_sh, m_sn;  // bytes
+  int Hq, group, Nq, Nk, D;
+  int mask_kind;  // 0 none, 1 causal, 2 dense
+  float scale;
+};
+
+constexpr int kRows = 4;
+constexpr int kChunk = 32;
+
+template <int DMAX>
+__global__ void __launch_bounds__(kRows * 32)
+    attn_fwd_f32_kernel(const F32Params p) {
+  extern __shared__ float sm[];
+  float* sK = sm;                                // [32][DMAX+1]
+  float* sV = sK + kChunk * (DMAX + 1);          // [32][DMAX]
+  float* sQ = sV + kChunk * DMAX;                // [4][DMAX]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int b = bh / p.Hq, h = bh - (bh / p.Hq) * p.Hq, hk = h / p.group;
+  const int row = blockIdx.x * kRows + warp;
+  const bool live = row < p.Nq;
+  const int D = p.D;
+
+  const float* Q = p.q + b * p.q_sb + h * p.q_sh;
+  const float* K = p.k + b * p.k_sb + hk * p.k_sh;
+  const float* V = p.v + b * p.v_sb + hk * p.v_sh;
+  for (int d = lane; d < D; d += 32) sQ[warp * DMAX + d] = live ? Q[row * p.q_sn + d] : 0.f;
+
+  constexpr int NO = DMAX / 32;
+  float o[NO];
+#pragma unroll
+  for (int i = 0; i < NO; ++i) o[i] = 0.f;
+  float m = -INFINITY, l = 0.f;
+
+  int kend = p.Nk;
+  if (p.mask_kind == 1) {
+    // Keys beyond the last row of this CTA are masked for every row in it.
+    const int last = min(blockIdx.x * kRows + kRows - 1, p.Nq - 1);
+    kend = min(p.Nk, last + 1);
+  }
+  for (int k0 = 0; k0 < kend; k0 += kChunk) {
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < kChunk * D; idx += blockDim.x) {
+      const int kr = idx / D, d = idx - (idx / D) * D;
+      const int key = k0 + kr;
+      const bool in = key < p.Nk;
+      sK[kr * (DMAX + 1) + d] = in ? K[key * p.k_sn + d] : 0.f;
+      sV[kr * DMAX + d] = in ? V[key * p.v_sn + d] : 0.f;
+    }
+    __syncthreads();
+    const int key = k0 + lane;
+    float s = 0.f;
+    for (int d = 0; d < D; ++d) s = fmaf(sQ[warp * DMAX + d], sK[lane * (DMAX + 1) + d], s);
+    s *= p.scale;
+    bool masked = key >= p.Nk;
+    if (p.mask_kind == 1) masked = masked || key > row;
+    if (p.mask_kind == 2 && live && key < p.Nk)
+      masked = masked || p.mask[b * p.m_sb + h * p.m_sh + row * p.m_sn + key] != 0;
+    if (masked) s = -INFINITY;
+    float mx = s;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const float m_new = fmaxf(m, mx);
+    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+    const float alpha = expf(m - m_use);
+    const float pr = expf(s - m_use);
+    float ps = pr;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+    l = l * alpha + ps;
+#pragma unroll
+    for (int i = 0; i < NO; ++i) o[i] *= alpha;
+    for (int kr = 0; kr < kChunk; ++kr) {
+      const float pk = __shfl_sync(0xffffffffu, pr, kr);
+#pragma unroll
+      for (int i = 0; i < NO; ++i) {
+        const int d = lane + 32 * i;
+        if (d < D) o[i] = fmaf(pk, sV[kr * DMAX + d], o[i]);
+      }
+    }
+    m = m_new;
+  }
+  if (live) {
+    float* O = p.o + b * p.o_sb + h * p.o_sh + row * p.o_sn;
+#pragma unroll
+    for (int i = 0; i < NO; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) O[d] = o[i] / l;
+    }
+    if (p.lse && lane == 0) p.lse[static_cast<int64_t>(bh) * p.Nq + row] = m + logf(l);
+  }
+}
+
+template <int DMAX>
+constexpr size_t f32_smem_bytes() {
+  return sizeof(float) * (kChunk * (DMAX + 1) + kChunk * DMAX + kRows * DMAX);
+}
+
+}  // namespace attn_f32

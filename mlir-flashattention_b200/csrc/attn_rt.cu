@@ -1,0 +1,716 @@
+// attn_rt.cu — host runtime behind include/attn_rt.h.
+//
+// This is the boundary where the reference's CPU lowering of `attention.fused`
+// (lib/Attention/TilingPass.cpp:155-392) is replaced: the op's operands arrive
+// here (as an AttnDesc or as MLIR memref descriptors), are checked with the
+// reference verifier's rules (lib/Attention/AttentionOps.cpp:33-59), and the
+// sm_100a kernels are launched.  No CPU fallback exists: without an sm_100
+// device every entry point returns ATTN_ERR_NO_DEVICE.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/attn_rt.h"
+#include "attn_fwd_f32.cuh"
+#include "attn_fwd_sm100.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<int64_t> g_launches{0};
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(ATTN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CUDA_TRY(call)                                   \
+  do {                                                   \
+    cudaError_t e_ = (call);                             \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);  \
+  } while (0)
+
+// ----------------------------------------------------------------- devices
+constexpr int kMaxDevices = 64;
+constexpr int kStageBufs = 2;
+
+struct Staging {
+  // One set of device buffers for a chunk of (batch, kv-head) groups.
+  void* q = nullptr;
+  void* k = nullptr;
+  void* v = nullptr;
+  void* o = nullptr;
+  float* lse = nullptr;
+  size_t q_bytes = 0, k_bytes = 0, v_bytes = 0, o_bytes = 0, lse_bytes = 0;
+  cudaEvent_t h2d_done = nullptr, comp_done = nullptr, d2h_done = nullptr;
+};
+
+struct DevState {
+  std::mutex mu;
+  bool ready = false;
+  int sm_count = 0;
+  int32_t* status = nullptr;
+  cudaStream_t s_compute = nullptr, s_h2d = nullptr, s_d2h = nullptr;
+  Staging stage[kStageBufs];
+};
+
+DevState g_dev[kMaxDevices];
+
+int init_device(int device) {
+  if (device < 0 || device >= kMaxDevices) return fail(ATTN_ERR_INVALID, "bad device %d", device);
+  DevState& st = g_dev[device];
+  std::lock_guard<std::mutex> lk(st.mu);
+  if (st.ready) return ATTN_OK;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= device)
+    return fail(ATTN_ERR_NO_DEVICE, "no CUDA device %d visible", device);
+  CUDA_TRY(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(ATTN_ERR_NO_DEVICE, "device %d is sm_%d%d; this runtime is built for sm_100a",
+                device, prop.major, prop.minor);
+  st.sm_count = prop.multiProcessorCount;
+  CUDA_TRY(cudaMalloc(&st.status, sizeof(int32_t)));
+  CUDA_TRY(cudaMemset(st.status, 0, sizeof(int32_t)));
+  CUDA_TRY(cudaStreamCreateWithFlags(&st.s_compute, cudaStreamNonBlocking));
+  CUDA_TRY(cudaStreamCreateWithFlags(&st.s_h2d, cudaStreamNonBlocking));
+  CUDA_TRY(cudaStreamCreateWithFlags(&st.s_d2h, cudaStreamNonBlocking));
+  for (auto& sb : st.stage) {
+    CUDA_TRY(cudaEventCreateWithFlags(&sb.h2d_done, cudaEventDisableTiming));
+    CUDA_TRY(cudaEventCreateWithFlags(&sb.comp_done, cudaEventDisableTiming));
+    CUDA_TRY(cudaEventCreateWithFlags(&sb.d2h_done, cudaEventDisableTiming));
+  }
+  st.ready = true;
+  return ATTN_OK;
+}
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return fail(ATTN_ERR_NO_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
+  return ATTN_OK;
+}
+
+// ------------------------------------------------------------ tensor maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 4-D map over (head_dim, rows, heads, batch) with a 128-byte x 128-row box
+// and 128-byte swizzle.  Strides in elements; a unit dimension gets a
+// synthetic stride (never stepped along).
+int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int eb, int64_t D,
+             int64_t N, int64_t H, int64_t B, int64_t s_n, int64_t s_h, int64_t s_b) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(ATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (N == 1) s_n = D;
+  if (H == 1) s_h = s_n * N;
+  if (B == 1) s_b = s_h * H;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N),
+                        static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_n * eb), static_cast<cuuint64_t>(s_h * eb),
+                           static_cast<cuuint64_t>(s_b * eb)};
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] % 16 != 0 || strides[i] >= (1ull << 40))
+      return fail(ATTN_ERR_ALIGN, "tensor stride %llu bytes is not a multiple of 16",
+                  static_cast<unsigned long long>(strides[i]));
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / eb), 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ATTN_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return ATTN_OK;
+}
+
+// -------------------------------------------------------------- launches
+template <int D, bool CAUSAL, bool FP8>
+int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
+  using C = attn_sm100::FwdCfg<D, FP8>;
+  auto kern = attn_sm100::attn_fwd_sm100_kernel<D, CAUSAL, FP8>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(C::kSmemBytes));
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute");
+  const CUtensorMapDataType dt =
+      FP8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int eb = FP8 ? 1 : 2;
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = make_map(&mq, d.q, dt, eb, d.D, d.Nq, d.Hq, d.B, d.q_stride[2], d.q_stride[1],
+                     d.q_stride[0])) != ATTN_OK)
+    return rc;
+  if ((rc = make_map(&mk, d.k, dt, eb, d.D, d.Nk, d.Hkv, d.B, d.k_stride[2], d.k_stride[1],
+                     d.k_stride[0])) != ATTN_OK)
+    return rc;
+  if ((rc = make_map(&mv, d.v, dt, eb, d.D, d.Nk, d.Hkv, d.B, d.v_stride[2], d.v_stride[1],
+                     d.v_stride[0])) != ATTN_OK)
+    return rc;
+  attn_sm100::FwdParams p{};
+  p.o = d.o;
+  p.o_sb = d.o_stride[0];
+  p.o_sh = d.o_stride[1];
+  p.o_sn = d.o_stride[2];
+  p.lse = d.lse;
+  p.status = status;
+  p.Hq = static_cast<int>(d.Hq);
+  p.group = static_cast<int>(d.Hq / d.Hkv);
+  p.Nq = static_cast<int>(d.Nq);
+  p.Nk = static_cast<int>(d.Nk);
+  p.num_pairs = static_cast<int>((d.Nq + 255) / 256);
+  float sl2 = d.scale * 1.4426950408889634f;
+  if (FP8) sl2 *= d.q_descale * d.k_descale;
+  if (sl2 == 0.f) sl2 = 1e-30f;  // scale 0: uniform weights without 0*inf
+  p.scale_log2 = sl2;
+  p.o_scale = FP8 ? d.v_descale : 1.f;
+  p.out_f32 = d.out_dtype == ATTN_F32 ? 1 : 0;
+  dim3 grid(static_cast<unsigned>(d.B * d.Hq), static_cast<unsigned>(p.num_pairs));
+  kern<<<grid, attn_sm100::kThreads, C::kSmemBytes, stream>>>(mq, mk, mv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_sm100 launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return ATTN_OK;
+}
+
+template <int DMAX>
+int launch_f32(const AttnDesc& d, cudaStream_t stream) {
+  auto kern = attn_f32::attn_fwd_f32_kernel<DMAX>;
+  constexpr size_t smem = attn_f32::f32_smem_bytes<DMAX>();
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem));
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute");
+  attn_f32::F32Params p{};
+  p.q = static_cast<const float*>(d.q);
+  p.k = static_cast<const float*>(d.k);
+  p.v = static_cast<const float*>(d.v);
+  p.o = static_cast<float*>(d.o);
+  p.lse = d.lse;
+  p.mask = d.mask;
+  p.q_sb = d.q_stride[0]; p.q_sh = d.q_stride[1]; p.q_sn = d.q_stride[2];
+  p.k_sb = d.k_stride[0]; p.k_sh = d.k_stride[1]; p.k_sn = d.k_stride[2];
+  p.v_sb = d.v_stride[0]; p.v_sh = d.v_stride[1]; p.v_sn = d.v_stride[2];
+  p.o_sb = d.o_stride[0]; p.o_sh = d.o_stride[1]; p.o_sn = d.o_stride[2];
+  p.m_sb = d.mask_stride[0]; p.m_sh = d.mask_stride[1]; p.m_sn = d.mask_stride[2];
+  p.Hq = static_cast<int>(d.Hq);
+  p.group = static_cast<int>(d.Hq / d.Hkv);
+  p.Nq = static_cast<int>(d.Nq);
+  p.Nk = static_cast<int>(d.Nk);
+  p.D = static_cast<int>(d.D);
+  p.mask_kind = d.mask_kind;
+  p.scale = d.scale;
+  dim3 grid(static_cast<unsigned>((d.Nq + attn_f32::kRows - 1) / attn_f32::kRows),
+            static_cast<unsigned>(d.B * d.Hq));
+  kern<<<grid, attn_f32::kRows * 32, smem, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_f32 launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return ATTN_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int validate(const AttnDesc& d) {
+  if (!d.q || !d.k || !d.v || !d.o) return fail(ATTN_ERR_INVALID, "null Q/K/V/output pointer");
+  if (d.flags != 0) return fail(ATTN_ERR_INVALID, "flags must be 0");
+  if (d.B <= 0 || d.Hq <= 0 || d.Hkv <= 0 || d.Nq <= 0 || d.Nk <= 0 || d.D <= 0)
+    return fail(ATTN_ERR_SHAPE, "all extents must be positive (B=%lld Hq=%lld Hkv=%lld Nq=%lld "
+                "Nk=%lld D=%lld)", (long long)d.B, (long long)d.Hq, (long long)d.Hkv,
+                (long long)d.Nq, (long long)d.Nk, (long long)d.D);
+  if (d.Hq % d.Hkv != 0)
+    return fail(ATTN_ERR_SHAPE, "query heads (%lld) must be a multiple of key/value heads (%lld)",
+                (long long)d.Hq, (long long)d.Hkv);
+  if (d.Nq >= (1ll << 31) || d.Nk >= (1ll << 31) || d.B * d.Hq >= (1ll << 31))
+    return fail(ATTN_ERR_SHAPE, "extent too large");
+  if (d.mask_kind < ATTN_MASK_NONE || d.mask_kind > ATTN_MASK_DENSE)
+    return fail(ATTN_ERR_INVALID, "unknown mask kind %d", d.mask_kind);
+  if (d.mask_kind == ATTN_MASK_DENSE && !d.mask)
+    return fail(ATTN_ERR_INVALID, "dense mask requested without a mask pointer");
+  if (!std::isfinite(d.scale)) return fail(ATTN_ERR_INVALID, "scale must be finite");
+  switch (d.dtype) {
+    case ATTN_F32:
+      if (d.out_dtype != ATTN_F32)
+        return fail(ATTN_ERR_DTYPE, "f32 inputs produce an f32 output");
+      if (d.D > 256) return fail(ATTN_ERR_UNSUPPORTED, "f32 path supports head_dim <= 256");
+      return ATTN_OK;
+    case ATTN_BF16:
+    case ATTN_E4M3: {
+      if (d.out_dtype != ATTN_BF16 && d.out_dtype != ATTN_F32)
+        return fail(ATTN_ERR_DTYPE, "output must be bf16 or f32");
+      if (d.dtype == ATTN_BF16 && d.D != 64 && d.D != 128)
+        return fail(ATTN_ERR_UNSUPPORTED, "bf16 path supports head_dim 64 or 128 (got %lld)",
+                    (long long)d.D);
+      if (d.dtype == ATTN_E4M3 && d.D != 128)
+        return fail(ATTN_ERR_UNSUPPORTED, "e4m3 path supports head_dim 128 (got %lld)",
+                    (long long)d.D);
+      if (d.mask_kind == ATTN_MASK_DENSE)
+        return fail(ATTN_ERR_UNSUPPORTED, "dense masks are supported on the f32 path only");
+      if (d.dtype == ATTN_E4M3 && !(d.q_descale > 0.f && d.k_descale > 0.f && d.v_descale > 0.f))
+        return fail(ATTN_ERR_INVALID, "e4m3 descales must be positive");
+      if (!aligned16(d.q) || !aligned16(d.k) || !aligned16(d.v) || !aligned16(d.o))
+        return fail(ATTN_ERR_ALIGN, "Q/K/V/output must be 16-byte aligned");
+      const int64_t ob = d.out_dtype == ATTN_F32 ? 4 : 2;
+      for (int i = 0; i < 3; ++i)
+        if ((d.o_stride[i] * ob) % 16 != 0 &&
+            !((i == 0 && d.B == 1) || (i == 1 && d.Hq == 1) || (i == 2 && d.Nq == 1)))
+          return fail(ATTN_ERR_ALIGN, "output strides must be multiples of 16 bytes");
+      return ATTN_OK;
+    }
+    default:
+      return fail(ATTN_ERR_DTYPE, "unknown dtype %d", d.dtype);
+  }
+}
+
+int dispatch(const AttnDesc& d, int32_t* status, cudaStream_t s) {
+  const bool causal = d.mask_kind == ATTN_MASK_CAUSAL;
+  if (d.dtype == ATTN_F32) {
+    if (d.D <= 64) return launch_f32<64>(d, s);
+    if (d.D <= 128) return launch_f32<128>(d, s);
+    return launch_f32<256>(d, s);
+  }
+  if (d.dtype == ATTN_BF16) {
+    if (d.D == 64) return causal ? launch_sm100<64, true, false>(d, status, s)
+                                 : launch_sm100<64, false, false>(d, status, s);
+    return causal ? launch_sm100<128, true, false>(d, status, s)
+                  : launch_sm100<128, false, false>(d, status, s);
+  }
+  return causal ? launch_sm100<128, true, true>(d, status, s)
+                : launch_sm100<128, false, true>(d, status, s);
+}
+
+// ------------------------------------------------- memref-descriptor layer
+struct View {
+  char* ptr = nullptr;
+  int64_t size[4] = {1, 1, 1, 1};   // B, H, N, D
+  int64_t stride[4] = {0, 0, 0, 1};
+};
+
+View view2(const AttnMemRef2D* m, int eb) {
+  View v;
+  v.ptr = static_cast<char*>(m->aligned) + m->offset * eb;
+  v.size[2] = m->sizes[0];
+  v.size[3] = m->sizes[1];
+  v.stride[2] = m->strides[0];
+  v.stride[3] = m->strides[1];
+  v.stride[1] = m->sizes[0] * m->strides[0];
+  v.stride[0] = v.stride[1];
+  return v;
+}
+
+View view4(const AttnMemRef4D* m, int eb) {
+  View v;
+  v.ptr = static_cast<char*>(m->aligned) + m->offset * eb;
+  for (int i = 0; i < 4; ++i) {
+    v.size[i] = m->sizes[i];
+    v.stride[i] = m->strides[i];
+  }
+  return v;
+}
+
+bool is_device_ptr(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// The reference verifier's shape rules (AttentionOps.cpp:48-56), extended to
+// batch/head extents; V's head_dim is also checked (the reference does not).
+int verify_views(const View& Q, const View& K, const View& V, const View& O) {
+  if (K.size[3] != Q.size[3]) return fail(ATTN_ERR_SHAPE, "K head_dim must equal Q head_dim");
+  if (V.size[2] != K.size[2]) return fail(ATTN_ERR_SHAPE, "V seq_len must equal K seq_len");
+  if (O.size[2] != Q.size[2]) return fail(ATTN_ERR_SHAPE, "output seq_q must equal Q seq_q");
+  if (O.size[3] != Q.size[3]) return fail(ATTN_ERR_SHAPE, "output head_dim must equal Q head_dim");
+  if (V.size[3] != Q.size[3]) return fail(ATTN_ERR_SHAPE, "V head_dim must equal Q head_dim");
+  if (K.size[0] != Q.size[0] || V.size[0] != Q.size[0] || O.size[0] != Q.size[0])
+    return fail(ATTN_ERR_SHAPE, "batch extents must match");
+  if (V.size[1] != K.size[1] || O.size[1] != Q.size[1])
+    return fail(ATTN_ERR_SHAPE, "head extents must match");
+  for (const View* v : {&Q, &K, &V, &O})
+    if (v->stride[3] != 1) return fail(ATTN_ERR_STRIDE, "head_dim must be the unit-stride dimension");
+  return ATTN_OK;
+}
+
+AttnDesc desc_from_views(int dtype, int out_dtype, int mask_kind, const View& Q, const View& K,
+                         const View& V, const View& O, float scale) {
+  AttnDesc d{};
+  d.dtype = dtype;
+  d.out_dtype = out_dtype;
+  d.mask_kind = mask_kind;
+  d.B = Q.size[0];
+  d.Hq = Q.size[1];
+  d.Hkv = K.size[1];
+  d.Nq = Q.size[2];
+  d.Nk = K.size[2];
+  d.D = Q.size[3];
+  for (int i = 0; i < 3; ++i) {
+    d.q_stride[i] = Q.stride[i];
+    d.k_stride[i] = K.stride[i];
+    d.v_stride[i] = V.stride[i];
+    d.o_stride[i] = O.stride[i];
+  }
+  d.q = Q.ptr;
+  d.k = K.ptr;
+  d.v = V.ptr;
+  d.o = O.ptr;
+  d.scale = scale;
+  d.q_descale = d.k_descale = d.v_descale = 1.f;
+  return d;
+}
+
+size_t elem_bytes(int dt) { return dt == ATTN_F32 ? 4 : dt == ATTN_BF16 ? 2 : 1; }
+
+int ensure(void** p, size_t* have, size_t need) {
+  if (*have >= need) return ATTN_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *have = 0;
+  CUDA_TRY(cudaMalloc(p, need));
+  *have = need;
+  return ATTN_OK;
+}
+
+// Copy `rows` x `D` elements of slice (b, h) between host and device, the
+// device side dense ([rows][D]).
+cudaError_t copy_slice(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
+                       size_t rows, cudaMemcpyKind kind, cudaStream_t s) {
+  return cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, kind, s);
+}
+
+// Run a call whose operands live in host memory: chunks of (batch, kv-head)
+// groups are staged through device buffers, with the H2D copy of chunk c+1,
+// the kernels of chunk c and the D2H copy of chunk c-1 overlapped on three
+// streams.  Synchronous: returns when O (and LSE) are in host memory.
+int run_staged(const AttnDesc& hd, int device) {
+  DevState& st = g_dev[device];
+  std::lock_guard<std::mutex> lk(st.mu);  // one staged call per device at a time
+  const size_t eb = elem_bytes(hd.dtype), ob = elem_bytes(hd.out_dtype);
+  const int64_t group = hd.Hq / hd.Hkv;
+  const int64_t ngroups = hd.B * hd.Hkv;
+  const int64_t per_chunk = std::max<int64_t>(1, (ngroups + 7) / 8);
+  const int64_t nchunks = (ngroups + per_chunk - 1) / per_chunk;
+  const size_t q_slice = static_cast<size_t>(hd.Nq * hd.D) * eb;
+  const size_t kv_slice = static_cast<size_t>(hd.Nk * hd.D) * eb;
+  const size_t o_slice = static_cast<size_t>(hd.Nq * hd.D) * ob;
+  for (auto& sb : st.stage) {
+    int rc;
+    if ((rc = ensure(&sb.q, &sb.q_bytes, q_slice * group * per_chunk)) != ATTN_OK) return rc;
+    if ((rc = ensure(&sb.k, &sb.k_bytes, kv_slice * per_chunk)) != ATTN_OK) return rc;
+    if ((rc = ensure(&sb.v, &sb.v_bytes, kv_slice * per_chunk)) != ATTN_OK) return rc;
+    if ((rc = ensure(&sb.o, &sb.o_bytes, o_slice * group * per_chunk)) != ATTN_OK) return rc;
+    if (hd.lse) {
+      void* l = sb.lse;
+      if ((rc = ensure(&l, &sb.lse_bytes, sizeof(float) * hd.Nq * group * per_chunk)) != ATTN_OK)
+        return rc;
+      sb.lse = static_cast<float*>(l);
+    }
+  }
+
+  for (int64_t c = 0; c < nchunks; ++c) {
+    Staging& sb = st.stage[c % kStageBufs];
+    const int64_t g0 = c * per_chunk;
+    const int64_t gn = std::min<int64_t>(per_chunk, ngroups - g0);
+    if (c >= kStageBufs) CUDA_TRY(cudaStreamWaitEvent(st.s_h2d, sb.d2h_done, 0));
+    for (int64_t g = 0; g < gn; ++g) {
+      const int64_t b = (g0 + g) / hd.Hkv, hk = (g0 + g) % hd.Hkv;
+      const char* ks = static_cast<const char*>(hd.k) + (b * hd.k_stride[0] + hk * hd.k_stride[1]) * eb;
+      const char* vs = static_cast<const char*>(hd.v) + (b * hd.v_stride[0] + hk * hd.v_stride[1]) * eb;
+      CUDA_TRY(copy_slice(static_cast<char*>(sb.k) + g * kv_slice, hd.D * eb, ks,
+                          hd.k_stride[2] * eb, hd.D * eb, hd.Nk, cudaMemcpyHostToDevice, st.s_h2d));
+      CUDA_TRY(copy_slice(static_cast<char*>(sb.v) + g * kv_slice, hd.D * eb, vs,
+                          hd.v_stride[2] * eb, hd.D * eb, hd.Nk, cudaMemcpyHostToDevice, st.s_h2d));
+      for (int64_t i = 0; i < group; ++i) {
+        const int64_t h = hk * group + i;
+        const char* qs = static_cast<const char*>(hd.q) + (b * hd.q_stride[0] + h * hd.q_stride[1]) * eb;
+        CUDA_TRY(copy_slice(static_cast<char*>(sb.q) + (g * group + i) * q_slice, hd.D * eb, qs,
+                            hd.q_stride[2] * eb, hd.D * eb, hd.Nq, cudaMemcpyHostToDevice,
+                            st.s_h2d));
+      }
+    }
+    CUDA_TRY(cudaEventRecord(sb.h2d_done, st.s_h2d));
+    CUDA_TRY(cudaStreamWaitEvent(st.s_compute, sb.h2d_done, 0));
+    // The chunk on the device is [gn, group, N, D] dense: B' = gn, Hq' = group, Hkv' = 1.
+    AttnDesc dd = hd;
+    dd.B = gn;
+    dd.Hq = group;
+    dd.Hkv = 1;
+    dd.q = sb.q;
+    dd.k = sb.k;
+    dd.v = sb.v;
+    dd.o = sb.o;
+    dd.lse = hd.lse ? sb.lse : nullptr;
+    dd.q_stride[2] = hd.D; dd.q_stride[1] = hd.Nq * hd.D; dd.q_stride[0] = group * hd.Nq * hd.D;
+    dd.o_stride[2] = hd.D; dd.o_stride[1] = hd.Nq * hd.D; dd.o_stride[0] = group * hd.Nq * hd.D;
+    dd.k_stride[2] = hd.D; dd.k_stride[1] = hd.Nk * hd.D; dd.k_stride[0] = hd.Nk * hd.D;
+    dd.v_stride[2] = hd.D; dd.v_stride[1] = hd.Nk * hd.D; dd.v_stride[0] = hd.Nk * hd.D;
+    dd.mask = nullptr;
+    if (hd.mask_kind == ATTN_MASK_DENSE)
+      return fail(ATTN_ERR_UNSUPPORTED, "dense masks on host memrefs are not staged");
+    int rc = validate(dd);
+    if (rc != ATTN_OK) return rc;
+    rc = dispatch(dd, st.status, st.s_compute);
+    if (rc != ATTN_OK) return rc;
+    CUDA_TRY(cudaEventRecord(sb.comp_done, st.s_compute));
+    CUDA_TRY(cudaStreamWaitEvent(st.s_d2h, sb.comp_done, 0));
+    for (int64_t g = 0; g < gn; ++g) {
+      const int64_t b = (g0 + g) / hd.Hkv, hk = (g0 + g) % hd.Hkv;
+      for (int64_t i = 0; i < group; ++i) {
+        const int64_t h = hk * group + i;
+        char* os = static_cast<char*>(hd.o) + (b * hd.o_stride[0] + h * hd.o_stride[1]) * ob;
+        CUDA_TRY(copy_slice(os, hd.o_stride[2] * ob,
+                            static_cast<char*>(sb.o) + (g * group + i) * o_slice, hd.D * ob,
+                            hd.D * ob, hd.Nq, cudaMemcpyDeviceToHost, st.s_d2h));
+        if (hd.lse) {
+          float* ls = hd.lse + (b * hd.Hq + h) * hd.Nq;
+          CUDA_TRY(cudaMemcpyAsync(ls, sb.lse + (g * group + i) * hd.Nq, sizeof(float) * hd.Nq,
+                                   cudaMemcpyDeviceToHost, st.s_d2h));
+        }
+      }
+    }
+    CUDA_TRY(cudaEventRecord(sb.d2h_done, st.s_d2h));
+  }
+  CUDA_TRY(cudaStreamSynchronize(st.s_d2h));
+  CUDA_TRY(cudaStreamSynchronize(st.s_compute));
+  int32_t code = 0;
+  CUDA_TRY(cudaMemcpy(&code, st.status, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  if (code != 0) {
+    CUDA_TRY(cudaMemset(st.status, 0, sizeof(int32_t)));
+    return fail(code, "kernel reported %s", attn_rt_status_string(code));
+  }
+  return ATTN_OK;
+}
+
+// Common body of every _mlir_ciface_ entry: device operands run in place on
+// the runtime's stream; host operands go through run_staged.
+int run_views(int dtype, int out_dtype, int mask_kind, const View& Q, const View& K,
+              const View& V, const View& O, float scale, float qd, float kd, float vd,
+              const View* L, const View* M) {
+  int rc = verify_views(Q, K, V, O);
+  if (rc != ATTN_OK) return rc;
+  int dev = 0;
+  if ((rc = current_device(&dev)) != ATTN_OK) return rc;
+  if ((rc = init_device(dev)) != ATTN_OK) return rc;
+  AttnDesc d = desc_from_views(dtype, out_dtype, mask_kind, Q, K, V, O, scale);
+  d.q_descale = qd;
+  d.k_descale = kd;
+  d.v_descale = vd;
+  if (L) {
+    if (L->size[0] != Q.size[0] || L->size[1] != Q.size[1] || L->size[2] != Q.size[2])
+      return fail(ATTN_ERR_SHAPE, "LSE must be [B, H, seq_q]");
+    if (L->stride[2] != 1 || L->stride[1] != Q.size[2] || L->stride[0] != Q.size[1] * Q.size[2])
+      return fail(ATTN_ERR_STRIDE, "LSE must be contiguous");
+    d.lse = reinterpret_cast<float*>(L->ptr);
+  }
+  if (M) {
+    if (M->size[2] != Q.size[2] || M->size[3] != K.size[2])
+      return fail(ATTN_ERR_SHAPE, "mask must be [seq_q, seq_k]");
+    if (M->stride[3] != 1) return fail(ATTN_ERR_STRIDE, "mask columns must be unit-stride");
+    d.mask = reinterpret_cast<const uint8_t*>(M->ptr);
+    d.mask_stride[0] = M->stride[0];
+    d.mask_stride[1] = M->stride[1];
+    d.mask_stride[2] = M->stride[2];
+  }
+  const bool dev_q = is_device_ptr(d.q);
+  if (dev_q) {
+    if (!is_device_ptr(d.k) || !is_device_ptr(d.v) || !is_device_ptr(d.o) ||
+        (d.lse && !is_device_ptr(d.lse)) || (d.mask && !is_device_ptr(d.mask)))
+      return fail(ATTN_ERR_INVALID, "operands mix host and device memory");
+    DevState& st = g_dev[dev];
+    if ((rc = attn_fwd(&d, st.s_compute)) != ATTN_OK) return rc;
+    return attn_rt_check_status(dev, st.s_compute);
+  }
+  if (d.mask_kind == ATTN_MASK_DENSE || d.dtype == ATTN_F32) {
+    // Small reference-shaped calls (f32, dense masks): stage whole operands.
+    const size_t eb = elem_bytes(d.dtype), ob = elem_bytes(d.out_dtype);
+    auto span = [](const int64_t* st, int64_t B, int64_t H, int64_t N, int64_t Dd) {
+      return ((B - 1) * st[0] + (H - 1) * st[1] + (N - 1) * st[2] + Dd);
+    };
+    const size_t qn = span(d.q_stride, d.B, d.Hq, d.Nq, d.D) * eb;
+    const size_t kn = span(d.k_stride, d.B, d.Hkv, d.Nk, d.D) * eb;
+    const size_t vn = span(d.v_stride, d.B, d.Hkv, d.Nk, d.D) * eb;
+    const size_t on = span(d.o_stride, d.B, d.Hq, d.Nq, d.D) * ob;
+    const size_t mn = d.mask ? static_cast<size_t>((d.B - 1) * d.mask_stride[0] +
+                                                   (d.Hq - 1) * d.mask_stride[1] +
+                                                   (d.Nq - 1) * d.mask_stride[2] + d.Nk)
+                             : 0;
+    const size_t ln = d.lse ? sizeof(float) * d.B * d.Hq * d.Nq : 0;
+    char* buf = nullptr;
+    const size_t total = qn + kn + vn + on + mn + ln + 6 * 256;
+    CUDA_TRY(cudaMalloc(&buf, total));
+    auto carve = [&](size_t n) { char* p = buf; buf += (n + 255) / 256 * 256; return p; };
+    char* base = buf;
+    char* dq = carve(qn); char* dk = carve(kn); char* dv = carve(vn); char* dout = carve(on);
+    char* dm = mn ? carve(mn) : nullptr;
+    char* dl = ln ? carve(ln) : nullptr;
+    DevState& st = g_dev[dev];
+    cudaStream_t s = st.s_compute;
+    auto cleanup = [&](int code) { cudaFree(base); return code; };
+    if (cudaMemcpyAsync(dq, d.q, qn, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(dk, d.k, kn, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(dv, d.v, vn, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        (dm && cudaMemcpyAsync(dm, d.mask, mn, cudaMemcpyHostToDevice, s) != cudaSuccess))
+      return cleanup(cuda_fail(cudaGetLastError(), "staging copy"));
+    AttnDesc dd = d;
+    dd.q = dq; dd.k = dk; dd.v = dv; dd.o = dout;
+    dd.mask = reinterpret_cast<const uint8_t*>(dm);
+    dd.lse = reinterpret_cast<float*>(dl);
+    if ((rc = attn_fwd(&dd, s)) != ATTN_OK) return cleanup(rc);
+    if (cudaMemcpyAsync(const_cast<void*>(static_cast<const void*>(d.o)), dout, on,
+                        cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        (dl && cudaMemcpyAsync(d.lse, dl, ln, cudaMemcpyDeviceToHost, s) != cudaSuccess))
+      return cleanup(cuda_fail(cudaGetLastError(), "staging copy back"));
+    rc = attn_rt_check_status(dev, s);
+    return cleanup(rc);
+  }
+  int vrc = validate(d);
+  if (vrc != ATTN_OK) return vrc;
+  return run_staged(d, dev);
+}
+
+}  // namespace
+
+// =================================================================== C ABI
+extern "C" {
+
+int attn_rt_version(void) { return (1 << 16) | 0; }
+
+int64_t attn_rt_launch_count(void) { return g_launches.load(); }
+
+const char* attn_rt_last_error(void) { return g_last_error.c_str(); }
+
+const char* attn_rt_status_string(int code) {
+  switch (code) {
+    case ATTN_OK: return "ok";
+    case ATTN_ERR_INVALID: return "invalid argument";
+    case ATTN_ERR_SHAPE: return "shape mismatch";
+    case ATTN_ERR_STRIDE: return "unsupported stride";
+    case ATTN_ERR_DTYPE: return "unsupported dtype";
+    case ATTN_ERR_ALIGN: return "misaligned pointer or stride";
+    case ATTN_ERR_CUDA: return "CUDA error";
+    case ATTN_ERR_TIMEOUT: return "device wait timed out";
+    case ATTN_ERR_UNSUPPORTED: return "unsupported variant";
+    case ATTN_ERR_NO_DEVICE: return "no sm_100 device";
+    default: return "unknown status";
+  }
+}
+
+int attn_rt_init(int device) { return init_device(device); }
+
+int attn_rt_check_status(int device, void* stream) {
+  int rc = init_device(device);
+  if (rc != ATTN_OK) return rc;
+  DevState& st = g_dev[device];
+  CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  int32_t code = 0;
+  CUDA_TRY(cudaMemcpy(&code, st.status, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  if (code != 0) {
+    CUDA_TRY(cudaMemset(st.status, 0, sizeof(int32_t)));
+    return fail(code, "kernel reported %s", attn_rt_status_string(code));
+  }
+  return ATTN_OK;
+}
+
+int attn_fwd(const AttnDesc* desc, void* stream) {
+  if (!desc) return fail(ATTN_ERR_INVALID, "null descriptor");
+  int rc = validate(*desc);
+  if (rc != ATTN_OK) return rc;
+  int dev = 0;
+  if ((rc = current_device(&dev)) != ATTN_OK) return rc;
+  if ((rc = init_device(dev)) != ATTN_OK) return rc;
+  int32_t* status = desc->status ? desc->status : g_dev[dev].status;
+  return dispatch(*desc, status, static_cast<cudaStream_t>(stream));
+}
+
+#define F32_2D(NAME, KIND)                                                                   \
+  int32_t NAME(AttnMemRef2D* Q, AttnMemRef2D* K, AttnMemRef2D* V, float scale,               \
+               AttnMemRef2D* O) {                                                            \
+    if (!Q || !K || !V || !O) return fail(ATTN_ERR_INVALID, "null memref descriptor");        \
+    return run_views(ATTN_F32, ATTN_F32, KIND, view2(Q, 4), view2(K, 4), view2(V, 4),         \
+                     view2(O, 4), scale, 1.f, 1.f, 1.f, nullptr, nullptr);                    \
+  }
+F32_2D(_mlir_ciface_attn_fused_f32_nomask, ATTN_MASK_NONE)
+F32_2D(_mlir_ciface_attn_fused_f32_causal, ATTN_MASK_CAUSAL)
+
+int32_t _mlir_ciface_attn_fused_f32_mask(AttnMemRef2D* Q, AttnMemRef2D* K, AttnMemRef2D* V,
+                                         float scale, AttnMemRef2D* mask, AttnMemRef2D* O) {
+  if (!Q || !K || !V || !O || !mask) return fail(ATTN_ERR_INVALID, "null memref descriptor");
+  View M = view2(mask, 1);
+  return run_views(ATTN_F32, ATTN_F32, ATTN_MASK_DENSE, view2(Q, 4), view2(K, 4), view2(V, 4),
+                   view2(O, 4), scale, 1.f, 1.f, 1.f, nullptr, &M);
+}
+
+#define F32_4D(NAME, KIND)                                                                   \
+  int32_t NAME(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V, float scale,               \
+               AttnMemRef4D* O) {                                                            \
+    if (!Q || !K || !V || !O) return fail(ATTN_ERR_INVALID, "null memref descriptor");        \
+    return run_views(ATTN_F32, ATTN_F32, KIND, view4(Q, 4), view4(K, 4), view4(V, 4),         \
+                     view4(O, 4), scale, 1.f, 1.f, 1.f, nullptr, nullptr);                    \
+  }
+F32_4D(_mlir_ciface_attn_fused_f32_nomask_4d, ATTN_MASK_NONE)
+F32_4D(_mlir_ciface_attn_fused_f32_causal_4d, ATTN_MASK_CAUSAL)
+
+#define BF16_4D(NAME, KIND)                                                                  \
+  int32_t NAME(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V, float scale,               \
+               AttnMemRef4D* O, AttnMemRef4D* LSE) {                                         \
+    if (!Q || !K || !V || !O) return fail(ATTN_ERR_INVALID, "null memref descriptor");        \
+    View L;                                                                                  \
+    if (LSE) L = view4(LSE, 4);                                                              \
+    return run_views(ATTN_BF16, ATTN_BF16, KIND, view4(Q, 2), view4(K, 2), view4(V, 2),       \
+                     view4(O, 2), scale, 1.f, 1.f, 1.f, LSE ? &L : nullptr, nullptr);         \
+  }
+BF16_4D(_mlir_ciface_attn_fused_bf16_nomask_4d, ATTN_MASK_NONE)
+BF16_4D(_mlir_ciface_attn_fused_bf16_causal_4d, ATTN_MASK_CAUSAL)
+
+#define E4M3_4D(NAME, KIND)                                                                  \
+  int32_t NAME(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V, float scale, float qd,     \
+               float kd, float vd, AttnMemRef4D* O, AttnMemRef4D* LSE) {                     \
+    if (!Q || !K || !V || !O) return fail(ATTN_ERR_INVALID, "null memref descriptor");        \
+    View L;                                                                                  \
+    if (LSE) L = view4(LSE, 4);                                                              \
+    return run_views(ATTN_E4M3, ATTN_BF16, KIND, view4(Q, 1), view4(K, 1), view4(V, 1),       \
+                     view4(O, 2), scale, qd, kd, vd, LSE ? &L : nullptr, nullptr);            \
+  }
+E4M3_4D(_mlir_ciface_attn_fused_e4m3_nomask_4d, ATTN_MASK_NONE)
+E4M3_4D(_mlir_ciface_attn_fused_e4m3_causal_4d, ATTN_MASK_CAUSAL)
+
+}  // extern "C"

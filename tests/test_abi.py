@@ -1,0 +1,85 @@
+"""The C-ABI library: loads, exports every symbol include/attn_rt.h declares,
+and rejects bad operands with the reference verifier's rules (no GPU needed:
+validation happens before any device call)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "attn_rt.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(\w+)\s*\([^;{]*\)\s*;", text)) - {"sizeof"})
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    assert "attn_fwd" in names and "_mlir_ciface_attn_fused_f32_mask" in names
+    assert len(names) >= 16
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    pkg.lib()
+    out = subprocess.run(["nm", "-D", "--defined-only", pkg.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if ln.strip()}
+    missing = [n for n in declared_functions() if n not in exported]
+    assert not missing, missing
+
+
+def test_version_and_status_strings(pkg):
+    L = pkg.lib()
+    assert L.attn_rt_version() >> 16 == 1
+    for code, text in pkg.STATUS.items():
+        assert L.attn_rt_status_string(code).decode() == text
+
+
+def _desc(pkg, **kw):
+    d = pkg.AttnDesc()
+    d.dtype, d.out_dtype, d.mask_kind = pkg.ATTN_BF16, pkg.ATTN_BF16, pkg.MASK_CAUSAL
+    d.B, d.Hq, d.Hkv, d.Nq, d.Nk, d.D = 1, 4, 2, 256, 256, 128
+    for s in (d.q_stride, d.o_stride):
+        s[0], s[1], s[2] = 4 * 256 * 128, 256 * 128, 128
+    for s in (d.k_stride, d.v_stride):
+        s[0], s[1], s[2] = 2 * 256 * 128, 256 * 128, 128
+    d.q = d.k = d.v = d.o = 0x10000
+    d.scale = 0.125
+    d.q_descale = d.k_descale = d.v_descale = 1.0
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize("field,value,code", [
+    ("Hkv", 3, -2),          # heads not a multiple
+    ("Nk", 0, -2),           # empty extent
+    ("D", 96, -8),           # bf16 head_dim not built
+    ("dtype", 7, -4),
+    ("mask_kind", 2, -1),    # dense without a mask pointer
+    ("q", 0x10008, -5),      # misaligned
+    ("flags", 1, -1),
+])
+def test_validation_codes(pkg, field, value, code):
+    L = pkg.lib()
+    d = _desc(pkg, **{field: value})
+    assert L.attn_fwd(ctypes.byref(d), None) == code
+    assert pkg.last_error()
+
+
+def test_null_descriptor(pkg):
+    assert pkg.lib().attn_fwd(None, None) == -1
+
+
+def test_no_device_is_reported_not_faked(pkg):
+    """On a machine without an sm_100 GPU a valid call fails loudly."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    d = _desc(pkg)
+    assert pkg.lib().attn_fwd(ctypes.byref(d), None) == -9

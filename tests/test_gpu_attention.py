@@ -1,0 +1,167 @@
+"""GPU parity tests: the sm_100a kernels (through the C ABI) against the oracle.
+
+Tolerances: max|O - O_oracle| / max|O_oracle| <= 1e-4 (f32), 2e-2 (bf16),
+6e-2 (e4m3); LSE max abs difference <= 1e-3 (1e-5 for f32).
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(got, ref):
+    return float(np.abs(got - ref).max() / np.abs(ref).max())
+
+
+def _run_pkg(pkg, wl, w, inp, causal, lse=True, out_f32=False):
+    q, k, v = wl.to_device(inp, w)
+    B, Hq, N, D = inp.q.shape
+    out = None
+    if out_f32:
+        out = torch.empty((B, Hq, N, D), dtype=torch.float32, device="cuda")
+    L = torch.empty((B, Hq, N), dtype=torch.float32, device="cuda") if lse else None
+    qd, kd, vd = inp.descale
+    out = pkg.fused(q, k, v, w.scale, output=out, causal=causal, lse=L,
+                    q_descale=qd, k_descale=kd, v_descale=vd)
+    pkg.check_status(0)
+    return out.float().cpu().numpy(), (L.cpu().numpy() if lse else None)
+
+
+def _ref(oracle, inp, w, causal, **kw):
+    return oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale, causal=causal, **kw)
+
+
+def test_f32_reference_config(pkg, wl, oracle):
+    """c1: the reference op's own form, f32 causal 128x64, scale 1/8."""
+    w = wl.WORKLOADS["c1"]
+    inp = wl.make_inputs(w)
+    got, lse = _run_pkg(pkg, wl, w, inp, causal=True)
+    ref, ref_lse = _ref(oracle, inp, w, True)
+    assert _rel(got, ref) <= 1e-4
+    assert np.abs(lse - ref_lse).max() <= 1e-5
+
+
+def test_f32_dense_mask_rank2_memref(pkg, wl, oracle):
+    """The rank-2 f32 memref entry with an explicit i1 mask, host buffers."""
+    rng = np.random.default_rng(11)
+    Nq, Nk, D = 96, 160, 32
+    Q, K, V = (rng.standard_normal((n, D)).astype(np.float32) for n in (Nq, Nk, Nk))
+    M = rng.random((Nq, Nk)) < 0.3
+    M[:, 0] = False  # keep every row partly visible
+    ref, _ = oracle.attn_fused_f32(Q, K, V, 0.2, mask=M)
+    tq, tk, tv = (torch.from_numpy(a) for a in (Q, K, V))
+    tm = torch.from_numpy(M.astype(np.uint8))
+    to = torch.zeros((Nq, D), dtype=torch.float32)
+    L = pkg.lib()
+    rc = L._mlir_ciface_attn_fused_f32_mask(pkg.memref(tq), pkg.memref(tk), pkg.memref(tv), 0.2,
+                                            pkg.memref(tm), pkg.memref(to))
+    assert rc == 0, pkg.last_error()
+    assert _rel(to.numpy(), ref) <= 1e-4
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("N", [128, 256, 384, 1000])
+def test_bf16_parity(pkg, wl, oracle, D, causal, N):
+    base = wl.WORKLOADS["c2"] if D == 64 else wl.WORKLOADS["c3"]
+    w = wl.Workload("t", "bf16", 2, 3, 3, N, D, causal, seed=100 + N + D)
+    inp = wl.make_inputs(w)
+    got, lse = _run_pkg(pkg, wl, w, inp, causal)
+    ref, ref_lse = _ref(oracle, inp, w, causal)
+    assert np.isfinite(got).all()
+    assert _rel(got, ref) <= base.tol
+    assert np.abs(lse - ref_lse).max() <= 1e-3
+
+
+def test_bf16_gqa_f32_output(pkg, wl, oracle):
+    w = wl.Workload("t", "bf16", 1, 8, 2, 512, 128, True, seed=7)
+    inp = wl.make_inputs(w)
+    got, _ = _run_pkg(pkg, wl, w, inp, True, out_f32=True)
+    ref, _ = _ref(oracle, inp, w, True)
+    assert _rel(got, ref) <= 2e-2
+
+
+def test_c2_full_config(pkg, wl, oracle):
+    """bf16 causal B=8 H=16 N=1024 D=64 over every slice."""
+    w = wl.WORKLOADS["c2"]
+    inp = wl.make_inputs(w)
+    got, lse = _run_pkg(pkg, wl, w, inp, True)
+    ref, ref_lse = _ref(oracle, inp, w, True)
+    assert _rel(got, ref) <= w.tol
+    assert np.abs(lse - ref_lse).max() <= 1e-3
+
+
+def test_e4m3_gqa_parity(pkg, wl, oracle):
+    """c5 shape family: e4m3 causal GQA (group 4), reduced to B=2, Hq=8, N=512."""
+    w = wl.WORKLOADS["c5"]
+    inp = wl.make_inputs(w, B=2, Hq=8, N=512)
+    got, lse = _run_pkg(pkg, wl, w, inp, True)
+    ref, ref_lse = _ref(oracle, inp, w, True)
+    assert _rel(got, ref) <= w.tol
+    assert np.abs(lse - ref_lse).max() <= 1e-2
+
+
+def test_c4_sampled_rows(pkg, wl, oracle):
+    """Full c4 size (bf16 causal B=1 H=32 N=16384 D=128): every output finite,
+    sampled Q tiles of the first and last head against the oracle."""
+    w = wl.WORKLOADS["c4"]
+    inp = wl.make_inputs(w)
+    got, lse = _run_pkg(pkg, wl, w, inp, True)
+    assert np.isfinite(got).all() and np.isfinite(lse).all()
+    ref = np.zeros_like(inp.qf)
+    ref_lse = np.zeros(inp.qf.shape[:3], np.float32)
+    oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale, causal=True, slices=[0, 31],
+                        tile_offset=3, tile_stride=16, out=ref, lse_out=ref_lse)
+    for h in (0, 31):
+        for t in range(3, 128, 16):
+            rows = slice(t * 128, t * 128 + 128)
+            g, r = got[0, h, rows], ref[0, h, rows]
+            assert _rel(g, r) <= w.tol, (h, t)
+            assert np.abs(lse[0, h, rows] - ref_lse[0, h, rows]).max() <= 1e-3
+
+
+def test_strided_operands_match_contiguous(pkg, wl):
+    """A [B, N, H, D] buffer viewed as [B, H, N, D] (non-contiguous heads)."""
+    w = wl.Workload("t", "bf16", 2, 4, 4, 256, 128, True, seed=5)
+    inp = wl.make_inputs(w)
+    q, k, v = wl.to_device(inp, w)
+    qs, ks, vs = (t.transpose(1, 2).contiguous().transpose(1, 2) for t in (q, k, v))
+    assert not qs.is_contiguous()
+    a = pkg.fused(q, k, v, w.scale, causal=True)
+    b = pkg.fused(qs, ks, vs, w.scale, causal=True)
+    pkg.check_status(0)
+    assert torch.equal(a, b)
+
+
+def test_host_memref_pipeline_equals_device(pkg, wl):
+    """The memref entry with pinned HOST buffers (staged, overlapped copies)
+    gives bit-identical results to the device-resident call."""
+    w = wl.Workload("t", "bf16", 2, 8, 8, 512, 128, True, seed=9)
+    inp = wl.make_inputs(w)
+    q, k, v = wl.to_device(inp, w)
+    L_dev = torch.empty((2, 8, 512), dtype=torch.float32, device="cuda")
+    ref = pkg.fused(q, k, v, w.scale, causal=True, lse=L_dev)
+    pkg.check_status(0)
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    ho = torch.empty_like(hq).pin_memory()
+    hl = torch.empty((2, 8, 512, 1), dtype=torch.float32).pin_memory()
+    L = pkg.lib()
+    rc = L._mlir_ciface_attn_fused_bf16_causal_4d(
+        pkg.memref(hq), pkg.memref(hk), pkg.memref(hv), w.scale, pkg.memref(ho), pkg.memref(hl))
+    assert rc == 0, pkg.last_error()
+    assert torch.equal(ho, ref.cpu())
+    assert torch.equal(hl[..., 0], L_dev.cpu())
+
+
+def test_unsupported_variants_raise(pkg):
+    q = torch.zeros((1, 1, 128, 96), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(pkg.AttentionError) as e:
+        pkg.fused(q, q, q, 0.1)
+    assert e.value.code == -8
+    q = torch.zeros((1, 1, 128, 64), dtype=torch.bfloat16, device="cuda")
+    o = torch.zeros((1, 1, 128, 72), dtype=torch.bfloat16, device="cuda")[..., :64]
+    with pytest.raises(pkg.AttentionError) as e:
+        pkg.fused(q, q, q, 0.1, output=o)
+    assert e.value.code == -5
