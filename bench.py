@@ -1,0 +1,421 @@
+"""Benchmark of the fused attention hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c4]
+                    [--scaling weak|strong] [--impl ours|reference]
+
+A step is one `attention.fused` call over the workload's (batch, head)
+slices.  Default workload: bf16 causal attention B=1, H=32, N=16384, d=128
+(scale 1/sqrt(128)), inputs N(0,1) drawn from a seeded generator.  With N GPUs
+(one process per GPU, torchrun) each rank owns an independent shard of
+slices; there is no collective in the timed region.  Weak scaling (default):
+every rank runs the full per-GPU workload, so the global batch is N x B.
+Strong scaling: the workload's slices are split across ranks.
+
+Metric: causal-adjusted attention TFLOP/s (4·N²·d per slice, halved when
+causal), whole job = all ranks' FLOPs / max-over-ranks device time.
+
+Keys beyond the base contract:
+  roofline      dominant kernel (attn_fwd_sm100) against the measured dense
+                bf16 peak; achieved from CUDA-event time of the timed region.
+  cpu_baseline  the oracle (CPU restatement of the reference's lowering)
+                on a bounded sample of the same workload, rank 0, N=1 only.
+  e2e           the same metric through the C ABI memref entry with pinned
+                HOST buffers (host->device copies of Q/K/V and device->host
+                copies of O/LSE inside the timed region).
+  clocks        SM clock and throttle reasons sampled (NVML) during the timed
+                region.
+`--impl reference` times the oracle on the host cores instead (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = ("causal attention TFLOP/s/GPU & % tensor peak at 1/2/4/8 B200 vs CPU-lowered ref")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def ncu_traffic(workload_name: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary for this workload (profiles/attn_fwd_sm100_<workload>.md), if any."""
+    path = os.path.join(ROOT, "profiles", f"attn_fwd_sm100_{workload_name}.md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML every ~10 ms."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.ok = [], set(), False
+        self.max_mhz = None
+        try:
+            import pynvml  # noqa: PLC0415
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # noqa: BLE001
+            self.ok = False
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.01)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self._t:
+            self._stop.set()
+            self._t.join()
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+def cpu_sample(w, budget_s=12.0, max_tiles=None):
+    """Time the oracle on c. `budget_s` of q tiles of the workload (all host
+    threads; one tile per thread per batch) and extrapolate to the workload.
+
+    The reference lowering computes every KV tile for every Q tile (no causal
+    skipping), so its cost per Q tile is uniform and the extrapolation is
+    exact up to timing noise.  Returns (TFLOP/s causal-adjusted, cores, text).
+    """
+    import numpy as np  # noqa: PLC0415
+    import __graft_entry__ as ge  # noqa: PLC0415
+
+    o = ge.oracle()
+    cores = o.max_threads()
+    rng = np.random.Generator(np.random.PCG64(w.seed))
+    # One (batch, head) slice of the workload's shape is enough: every slice
+    # costs the same.
+    q = rng.standard_normal((1, 1, w.N, w.D), dtype=np.float32)
+    k = rng.standard_normal((1, 1, w.N, w.D), dtype=np.float32)
+    v = rng.standard_normal((1, 1, w.N, w.D), dtype=np.float32)
+    out = np.zeros_like(q)
+    ntiles = math.ceil(w.N / 128)
+    done, t0, off = 0, time.perf_counter(), 0
+    while True:
+        stride = max(1, ntiles // cores)
+        o.attn_batched(q, k, v, w.scale, causal=w.causal, tile_offset=off % stride,
+                       tile_stride=stride, out=out, nthreads=cores)
+        done += len(range(off % stride, ntiles, stride))
+        off += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or (max_tiles and done >= max_tiles):
+            break
+    total_tiles = ntiles * w.slices
+    t_full = el * total_tiles / done
+    tflops = w.flops() / t_full / 1e12
+    text = (f"{done} of {total_tiles} Q tiles (128 rows x {w.N} keys, one slice of the "
+            f"workload's shape) in {el:.1f} s, extrapolated by tile count")
+    return tflops, cores, text
+
+
+def reference_arm(args, w, world):
+    """--impl reference: the oracle on the host cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np  # noqa: PLC0415
+    import __graft_entry__ as ge  # noqa: PLC0415
+
+    o = ge.oracle()
+    cores = o.max_threads()
+    rng = np.random.Generator(np.random.PCG64(w.seed))
+    q = rng.standard_normal((1, 1, w.N, w.D), dtype=np.float32)
+    k = rng.standard_normal((1, 1, w.N, w.D), dtype=np.float32)
+    v = rng.standard_normal((1, 1, w.N, w.D), dtype=np.float32)
+    out = np.zeros_like(q)
+    ntiles = math.ceil(w.N / 128)
+    per_step = min(ntiles, cores)
+    stride = max(1, ntiles // per_step)
+
+    def step(i):
+        o.attn_batched(q, k, v, w.scale, causal=w.causal, tile_offset=i % stride,
+                       tile_stride=stride, out=out, nthreads=cores)
+        return len(range(i % stride, ntiles, stride))
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    tiles = sum(step(args.warmup + i) for i in range(args.steps))
+    el = time.perf_counter() - t0
+    glob_slices = w.slices * (world if args.scaling == "weak" else 1)
+    t_full = el * (ntiles * glob_slices) / tiles
+    value = w.flops(glob_slices) / t_full / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))",
+        "config": config_dict(w, world, args),
+        "cpu_baseline": {
+            "value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": (f"each step = {per_step} Q tiles of one slice (128 rows x {w.N} keys); "
+                       f"reference-lowering restatement (oracle/attn_ref.cpp), no causal tile "
+                       f"skipping as in TilingPass; time extrapolated to the workload by tile "
+                       f"count; the MLIR CPU pipeline itself cannot be built here (no MLIR)"),
+        },
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def config_dict(w, world, args):
+    per_rank_b = w.B
+    return {
+        "workload": w.name, "global_batch": per_rank_b * world if args.scaling == "weak" else w.B,
+        "heads_q": w.Hq, "heads_kv": w.Hkv, "seq_len": w.N, "head_dim": w.D,
+        "causal": w.causal, "scale": w.scale, "parallelism": f"slice-shard x{world}",
+        "l2": "inputs larger than L2 (Q+K+V per GPU > 126 MB); no flush"
+        if w.bytes() > 126e6 else "L2 flushed between steps",
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c4")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="override the query-head count (reduced profiling case)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    import __graft_entry__ as ge  # noqa: PLC0415
+
+    pkg = ge.package()
+    from mlir_flashattention_b200 import workloads as wlmod  # noqa: PLC0415
+
+    w = wlmod.WORKLOADS[args.workload]
+    if args.heads:
+        import dataclasses  # noqa: PLC0415
+        w = dataclasses.replace(w, name=f"{w.name}_h{args.heads}", Hq=args.heads,
+                                Hkv=max(1, args.heads * w.Hkv // w.Hq))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        return reference_arm(args, w, world)
+
+    import torch  # noqa: PLC0415
+    import torch.distributed as dist  # noqa: PLC0415
+
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime  # noqa: PLC0415
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    # This rank's shard of (batch, head) slices.
+    if args.scaling == "weak":
+        B, Hq, Hkv = w.B, w.Hq, w.Hkv
+    else:
+        a, b = pkg.shard_slices(w.B * w.Hkv, world, rank)  # whole GQA groups
+        B, Hkv = 1, b - a
+        Hq = Hkv * (w.Hq // w.Hkv)
+        assert w.B == 1 or Hkv > 0, "strong scaling shards kv heads of batch 1"
+    slices = B * Hq
+    g = torch.Generator(device=dev)
+    g.manual_seed(w.seed * 1000 + rank)
+    dt = {"bf16": torch.bfloat16, "f32": torch.float32, "e4m3": torch.float8_e4m3fn}[w.dtype]
+
+    def rnd(h):
+        x = torch.randn((B, h, w.N, w.D), generator=g, device=dev, dtype=torch.float32) * w.std
+        if w.dtype == "e4m3":
+            s = x.abs().max() / 448.0
+            return (x / s).to(dt), float(s)
+        return x.to(dt), 1.0
+
+    (q, qd), (k, kd), (v, vd) = rnd(Hq), rnd(Hkv), rnd(Hkv)
+    odt = torch.float32 if w.dtype == "f32" else torch.bfloat16
+    out = torch.empty((B, Hq, w.N, w.D), dtype=odt, device=dev)
+    lse = torch.empty((B, Hq, w.N), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        pkg.fused(q, k, v, w.scale, output=out, causal=w.causal, lse=lse, q_descale=qd,
+                  k_descale=kd, v_descale=vd, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    pkg.check_status(local, stream)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    if clocks:
+        clocks.start()
+    n0 = pkg.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    launches = pkg.launch_count() - n0
+    clk = clocks.stop() if clocks else None
+    pkg.check_status(local, stream)
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_step = ms_max / args.steps
+    job_flops = w.flops(slices) * world  # every rank holds the same shard size
+    if args.scaling == "strong":
+        job_flops = w.flops()
+    value = job_flops / (ms_step * 1e-3) / 1e12
+
+    # ---- e2e through the C ABI with pinned host buffers.
+    e2e = None
+    if args.e2e_steps > 0:
+        e2e = run_e2e(args, pkg, w, q, k, v, out, (qd, kd, vd), B, Hq, job_flops, world, dev,
+                      odt, dist)
+
+    if rank == 0:
+        emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(args, pkg, w, q, k, v, out, descales, B, Hq, job_flops, world, dev, odt, dist):
+    import torch  # noqa: PLC0415
+
+    qd, kd, vd = descales
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    ho = torch.empty(out.shape, dtype=odt).pin_memory()
+    hl = torch.empty((B, Hq, w.N, 1), dtype=torch.float32).pin_memory()
+    L = pkg.lib()
+    if w.dtype == "bf16":
+        fn = L._mlir_ciface_attn_fused_bf16_causal_4d if w.causal else \
+            L._mlir_ciface_attn_fused_bf16_nomask_4d
+        call = lambda: fn(pkg.memref(hq), pkg.memref(hk), pkg.memref(hv), w.scale,  # noqa: E731
+                          pkg.memref(ho), pkg.memref(hl))
+    elif w.dtype == "e4m3":
+        fn = L._mlir_ciface_attn_fused_e4m3_causal_4d if w.causal else \
+            L._mlir_ciface_attn_fused_e4m3_nomask_4d
+        hq, hk, hv = (x.view(torch.uint8) for x in (hq, hk, hv))
+        call = lambda: fn(pkg.memref(hq), pkg.memref(hk), pkg.memref(hv), w.scale, qd, kd, vd,  # noqa: E731
+                          pkg.memref(ho), pkg.memref(hl))
+    else:
+        fn = L._mlir_ciface_attn_fused_f32_causal_4d if w.causal else \
+            L._mlir_ciface_attn_fused_f32_nomask_4d
+        call = lambda: fn(pkg.memref(hq), pkg.memref(hk), pkg.memref(hv), w.scale,  # noqa: E731
+                          pkg.memref(ho))
+    rc = call()  # warm-up (allocates the staging buffers once)
+    if rc != 0:
+        raise RuntimeError(f"e2e call failed: {pkg.last_error()}")
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        rc = call()
+        if rc != 0:
+            raise RuntimeError(f"e2e call failed: {pkg.last_error()}")
+    e2e_s = (time.perf_counter() - t0) / args.e2e_steps
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = job_flops / float(te.item()) / 1e12
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
+    d2h = ho.numel() * ho.element_size() + (hl.numel() * 4 if w.dtype != "f32" else 0)
+    return {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "path": "_mlir_ciface_attn_fused_*_4d with pinned host memrefs"}
+
+
+def emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e):
+    peaks, peak_src = load_peaks()
+    kernel_ms = ms / args.steps  # one launch per step on this rank
+    achieved = w.flops(slices) / (kernel_ms * 1e-3) / 1e12
+    sustained = ms * 1e-3 > 1.0
+    peak = peaks["bf16_tflops_sustained" if sustained else "bf16_tflops"]
+    if w.dtype == "e4m3":
+        peak = 2 * peak  # dense fp8 rate is twice bf16 on this part (nominal ratio)
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+        "dtype": w.dtype, "data": "synthetic (seeded N(0,1))",
+        "config": config_dict(w, world, args),
+        "tensor_peak_frac_per_gpu": value / world / peak,
+        "roofline": {
+            "bound": "tensor", "kernel": "attn_fwd_sm100_kernel",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak,
+            "peak_source": f"{peak_src} {'sustained' if sustained else 'burst'} dense bf16"
+            + (" x2 (fp8)" if w.dtype == "e4m3" else ""),
+            "traffic": ncu_traffic(w.name),
+            "algorithmic_bytes": w.bytes() * slices // w.slices,
+        },
+        "e2e": e2e,
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        tf, cores, text = cpu_sample(w)
+        line["cpu_baseline"] = {"value": tf, "unit": "TFLOP/s", "cores": cores,
+                                "kind": "port", "sample": text}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -161,7 +161,7 @@ def test_unsupported_variants_raise(pkg):
         pkg.fused(q, q, q, 0.1)
     assert e.value.code == -8
     q = torch.zeros((1, 1, 128, 64), dtype=torch.bfloat16, device="cuda")
-    o = torch.zeros((1, 1, 128, 72), dtype=torch.bfloat16, device="cuda")[..., :64]
+    o = torch.zeros((1, 1, 128, 68), dtype=torch.bfloat16, device="cuda")[..., :64]
     with pytest.raises(pkg.AttentionError) as e:
         pkg.fused(q, q, q, 0.1, output=o)
     assert e.value.code == -5
