@@ -154,8 +154,8 @@ ATTN_API int32_t _mlir_ciface_attn_fused_f32_nomask_4d(AttnMemRef4D* Q, AttnMemR
 ATTN_API int32_t _mlir_ciface_attn_fused_f32_causal_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
                                               float scale, AttnMemRef4D* O);
 
-/* Rank-4 bf16 in / bf16 out; LSE may be NULL or a memref<BxHxNqxf32> given as
- * a 4-D descriptor whose last size is 1. */
+/* Rank-4 bf16 in / bf16 out.  LSE is NULL, a zero-sized memref (not
+ * requested; what the lowering pass passes), or memref<BxHxNqx1xf32>. */
 ATTN_API int32_t _mlir_ciface_attn_fused_bf16_nomask_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
                                                float scale, AttnMemRef4D* O, AttnMemRef4D* LSE);
 ATTN_API int32_t _mlir_ciface_attn_fused_bf16_causal_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,

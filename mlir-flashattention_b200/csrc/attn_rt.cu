@@ -534,6 +534,7 @@ int run_views(int dtype, int out_dtype, int mask_kind, const View& Q, const View
   d.q_descale = qd;
   d.k_descale = kd;
   d.v_descale = vd;
+  if (L && L->size[0] * L->size[1] * L->size[2] * L->size[3] == 0) L = nullptr;  // not requested
   if (L) {
     if (L->size[0] != Q.size[0] || L->size[1] != Q.size[1] || L->size[2] != Q.size[2])
       return fail(ATTN_ERR_SHAPE, "LSE must be [B, H, seq_q]");
