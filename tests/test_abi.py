@@ -15,6 +15,7 @@ HEADER = os.path.join(ROOT, "include", "attn_rt.h")
 def declared_functions():
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = "\n".join(ln for ln in text.splitlines() if not ln.lstrip().startswith("#"))
     return sorted(set(re.findall(r"\b(\w+)\s*\([^;{]*\)\s*;", text)) - {"sizeof"})
 
 
