@@ -169,6 +169,37 @@ ATTN_API int32_t _mlir_ciface_attn_fused_e4m3_causal_4d(AttnMemRef4D* Q, AttnMem
                                                float scale, float q_descale, float k_descale,
                                                float v_descale, AttnMemRef4D* O, AttnMemRef4D* LSE);
 
+/* ---- entry point that allocates no device memory -------------------------
+ * No counterpart in the reference.
+ *
+ * Same operation as the memref entries above on HOST buffers (desc->q, k, v,
+ * o and lse are host pointers; dtype f32, bf16 or e4m3; mask kind none or
+ * causal), but without any device allocation.  It is meant for callers that
+ * cannot call cudaMalloc: e.g. a host program (such as MLIR-lowered CPU code
+ * operating on host memrefs) running in a process whose device memory is
+ * already reserved by another allocator (a serving engine or framework
+ * caching allocator that holds nearly all HBM), or one that must not take the
+ * implicit device synchronisation cudaMalloc/cudaFree may cause.
+ *
+ * Its device scratch — the kernel status word and the staging buffers for
+ * Q, K, V, O and LSE — is one file-scope __device__ array of
+ * ATTN_NOALLOC_SCRATCH_BYTES, which every GPU that loads the library holds
+ * until the process exits.  Work is staged through it in chunks of whole
+ * (batch, kv-head) groups; a call whose single group needs more than
+ * ATTN_NOALLOC_SCRATCH_BYTES - 256 bytes is rejected with ATTN_ERR_SHAPE and
+ * a message giving both sizes.
+ *
+ * The first call on each device resolves the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture.  Copies and kernels run on `stream` and the call
+ * returns after O (and LSE) are back in host memory.  All calls share the one
+ * array, which keeps the previous call's contents (the status word is
+ * cleared at the start of each call): calls that overlap on the GPU — from
+ * several threads or streams of one process — race and must be serialised by
+ * the caller.  Calls no cudaMalloc, cudaFree or allocating library routine. */
+#define ATTN_NOALLOC_SCRATCH_BYTES (64u << 20)
+ATTN_API int attn_fwd_host_noalloc(const AttnDesc* desc, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

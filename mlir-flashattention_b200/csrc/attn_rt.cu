@@ -715,3 +715,145 @@ E4M3_4D(_mlir_ciface_attn_fused_e4m3_nomask_4d, ATTN_MASK_NONE)
 E4M3_4D(_mlir_ciface_attn_fused_e4m3_causal_4d, ATTN_MASK_CAUSAL)
 
 }  // extern "C"
+
+// ======================================================= no-allocation entry
+// attn_fwd_host_noalloc: the host-buffer call of the memref entries, for
+// callers that must not allocate device memory.  Its device scratch (the
+// kernel status word and the staging buffers for Q, K, V, O and LSE) lives
+// in the file-scope array below instead of in cudaMalloc'd buffers.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = ATTN_NOALLOC_SCRATCH_BYTES;
+constexpr size_t kNoAllocStatusBytes = 256;  // status word, padded to 256 B
+
+// Module-scope device memory: every GPU that loads this library holds these
+// bytes until the process exits.  In host code `g_noalloc_scratch` only names
+// the symbol; its device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocDev {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  unsigned char* ptr = nullptr;  // device address of g_noalloc_scratch
+  int major = 0;
+};
+NoAllocDev g_noalloc[kMaxDevices];
+
+// Once per device, with that device current: check the architecture and
+// resolve the array's device address.  Allocates nothing.
+int noalloc_setup(int device, unsigned char** out) {
+  if (device < 0 || device >= kMaxDevices) return fail(ATTN_ERR_INVALID, "bad device %d", device);
+  NoAllocDev& nd = g_noalloc[device];
+  std::call_once(nd.once, [&] {
+    int major = 0;
+    nd.err = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    nd.major = major;
+    if (nd.err == cudaSuccess && major == 10)
+      nd.err = cudaGetSymbolAddress(reinterpret_cast<void**>(&nd.ptr), g_noalloc_scratch);
+  });
+  if (nd.err != cudaSuccess) return cuda_fail(nd.err, "attn_fwd_host_noalloc set-up");
+  if (nd.major != 10)
+    return fail(ATTN_ERR_NO_DEVICE, "device %d is not sm_100; attn_fwd_host_noalloc needs one",
+                device);
+  *out = nd.ptr;
+  return ATTN_OK;
+}
+
+size_t round256(size_t n) { return (n + 255) / 256 * 256; }
+
+}  // namespace
+
+extern "C" int attn_fwd_host_noalloc(const AttnDesc* desc, void* stream_) {
+  if (!desc) return fail(ATTN_ERR_INVALID, "null descriptor");
+  const AttnDesc& hd = *desc;
+  if (hd.mask_kind == ATTN_MASK_DENSE)
+    return fail(ATTN_ERR_UNSUPPORTED, "attn_fwd_host_noalloc supports no-mask and causal calls");
+  int rc = validate(hd);
+  if (rc != ATTN_OK) return rc;
+  int dev = 0;
+  if ((rc = current_device(&dev)) != ATTN_OK) return rc;
+  unsigned char* base = nullptr;
+  if ((rc = noalloc_setup(dev, &base)) != ATTN_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream_);
+
+  // Scratch needed per (batch, kv-head) group: the group's q-heads of Q, O
+  // and LSE, and its one kv-head of K and V, each region 256-byte aligned.
+  const size_t eb = elem_bytes(hd.dtype), ob = elem_bytes(hd.out_dtype);
+  const int64_t group = hd.Hq / hd.Hkv;
+  const int64_t ngroups = hd.B * hd.Hkv;
+  const size_t q_slice = static_cast<size_t>(hd.Nq * hd.D) * eb;
+  const size_t kv_slice = static_cast<size_t>(hd.Nk * hd.D) * eb;
+  const size_t o_slice = static_cast<size_t>(hd.Nq * hd.D) * ob;
+  const size_t l_slice = hd.lse ? sizeof(float) * static_cast<size_t>(hd.Nq) : 0;
+  const size_t per_group =
+      round256(group * q_slice) + 2 * round256(kv_slice) + round256(group * o_slice) +
+      round256(group * l_slice);
+  const size_t room = kNoAllocScratchBytes - kNoAllocStatusBytes;
+  if (per_group > room)
+    return fail(ATTN_ERR_SHAPE,
+                "attn_fwd_host_noalloc: one (batch, kv-head) group needs %zu bytes of device "
+                "scratch but the static scratch holds %zu bytes (ATTN_NOALLOC_SCRATCH_BYTES "
+                "minus %zu for the status word); use the memref entries instead",
+                per_group, room, kNoAllocStatusBytes);
+  const int64_t per_chunk = std::min<int64_t>(ngroups, static_cast<int64_t>(room / per_group));
+
+  int32_t* status = reinterpret_cast<int32_t*>(base);
+  // The array keeps the previous call's contents: the status word must start
+  // at zero.  (Staging regions are fully overwritten before they are read.)
+  CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int32_t), s));
+  unsigned char* dq = base + kNoAllocStatusBytes;
+  unsigned char* dk = dq + round256(per_chunk * group * q_slice);
+  unsigned char* dv = dk + round256(per_chunk * kv_slice);
+  unsigned char* dout = dv + round256(per_chunk * kv_slice);
+  float* dl = reinterpret_cast<float*>(dout + round256(per_chunk * group * o_slice));
+
+  for (int64_t g0 = 0; g0 < ngroups; g0 += per_chunk) {
+    const int64_t gn = std::min<int64_t>(per_chunk, ngroups - g0);
+    for (int64_t g = 0; g < gn; ++g) {
+      const int64_t b = (g0 + g) / hd.Hkv, hk = (g0 + g) % hd.Hkv;
+      const char* ks = static_cast<const char*>(hd.k) + (b * hd.k_stride[0] + hk * hd.k_stride[1]) * eb;
+      const char* vs = static_cast<const char*>(hd.v) + (b * hd.v_stride[0] + hk * hd.v_stride[1]) * eb;
+      CUDA_TRY(cudaMemcpy2DAsync(dk + g * kv_slice, hd.D * eb, ks, hd.k_stride[2] * eb,
+                                 hd.D * eb, hd.Nk, cudaMemcpyHostToDevice, s));
+      CUDA_TRY(cudaMemcpy2DAsync(dv + g * kv_slice, hd.D * eb, vs, hd.v_stride[2] * eb,
+                                 hd.D * eb, hd.Nk, cudaMemcpyHostToDevice, s));
+      for (int64_t i = 0; i < group; ++i) {
+        const int64_t h = hk * group + i;
+        const char* qs = static_cast<const char*>(hd.q) + (b * hd.q_stride[0] + h * hd.q_stride[1]) * eb;
+        CUDA_TRY(cudaMemcpy2DAsync(dq + (g * group + i) * q_slice, hd.D * eb, qs,
+                                   hd.q_stride[2] * eb, hd.D * eb, hd.Nq,
+                                   cudaMemcpyHostToDevice, s));
+      }
+    }
+    AttnDesc dd = hd;
+    dd.B = gn;
+    dd.Hq = group;
+    dd.Hkv = 1;
+    dd.q = dq; dd.k = dk; dd.v = dv; dd.o = dout;
+    dd.lse = hd.lse ? dl : nullptr;
+    dd.q_stride[2] = hd.D; dd.q_stride[1] = hd.Nq * hd.D; dd.q_stride[0] = group * hd.Nq * hd.D;
+    dd.o_stride[2] = hd.D; dd.o_stride[1] = hd.Nq * hd.D; dd.o_stride[0] = group * hd.Nq * hd.D;
+    dd.k_stride[2] = hd.D; dd.k_stride[1] = hd.Nk * hd.D; dd.k_stride[0] = hd.Nk * hd.D;
+    dd.v_stride[2] = hd.D; dd.v_stride[1] = hd.Nk * hd.D; dd.v_stride[0] = hd.Nk * hd.D;
+    dd.status = status;
+    if ((rc = validate(dd)) != ATTN_OK) return rc;
+    if ((rc = dispatch(dd, status, s)) != ATTN_OK) return rc;
+    for (int64_t g = 0; g < gn; ++g) {
+      const int64_t b = (g0 + g) / hd.Hkv, hk = (g0 + g) % hd.Hkv;
+      for (int64_t i = 0; i < group; ++i) {
+        const int64_t h = hk * group + i;
+        char* os = static_cast<char*>(hd.o) + (b * hd.o_stride[0] + h * hd.o_stride[1]) * ob;
+        CUDA_TRY(cudaMemcpy2DAsync(os, hd.o_stride[2] * ob, dout + (g * group + i) * o_slice,
+                                   hd.D * ob, hd.D * ob, hd.Nq, cudaMemcpyDeviceToHost, s));
+        if (hd.lse)
+          CUDA_TRY(cudaMemcpyAsync(hd.lse + (b * hd.Hq + h) * hd.Nq, dl + (g * group + i) * hd.Nq,
+                                   sizeof(float) * hd.Nq, cudaMemcpyDeviceToHost, s));
+      }
+    }
+  }
+  int32_t code = 0;
+  CUDA_TRY(cudaMemcpyAsync(&code, status, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  CUDA_TRY(cudaStreamSynchronize(s));
+  if (code != 0) return fail(code, "kernel reported %s", attn_rt_status_string(code));
+  return ATTN_OK;
+}
