@@ -245,51 +245,61 @@ __global__ void __launch_bounds__(kThreads, 1)
             issue_S(t, 0);
             mma_commit(&s_full[t]);
           }
+        mma_commit(&kv_empty[0]);  // K_0 is free once both S GEMMs finish
       }
+      // Per KV step j, for each Q tile t in turn: O_t += P_t(j)·V_j, then
+      // S_t(j+1) = Q_t·K_{j+1}ᵀ as soon as that P·V GEMM has finished reading
+      // P_t(j) (P lives in the S_t columns).  Tile t's next softmax can then
+      // start while the tensor cores run the other tile's GEMMs, so the two
+      // softmax warpgroups alternate with the tensor pipe.
       for (int j = 0; j < nmax && ok; ++j) {
-        const int ks = (2 * j) % C::kStages;
         const int vs = (2 * j + 1) % C::kStages;
         const uint32_t vu = static_cast<uint32_t>((2 * j + 1) / C::kStages);
-        mma_commit(&kv_empty[ks]);  // K_j is free once the S GEMMs finish
+        const int nks = (2 * j + 2) % C::kStages;
+        const uint32_t nku = static_cast<uint32_t>((2 * j + 2) / C::kStages);
+        bool k_next = false;
         if (!mbar_wait_bounded(&kv_full[vs], vu & 1u, abort_flag, p.status, kWaitLimitNs)) {
           ok = false;
           break;
         }
         for (int t = 0; t < 2 && ok; ++t) {
-          if (j < n_t[t]) {
-            if (!mbar_wait_bounded(&p_ready[t], static_cast<uint32_t>(j & 1), abort_flag,
-                                   p.status, kWaitLimitNs)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_PV(t, vs, j > 0);
-            mma_commit(&pv_done[t]);
-          }
-        }
-        if (!ok) break;
-        mma_commit(&kv_empty[vs]);  // V_j is free once the P·V GEMMs finish
-        if (j + 1 < nmax) {
-          const int nks = (2 * j + 2) % C::kStages;
-          const uint32_t nku = static_cast<uint32_t>((2 * j + 2) / C::kStages);
-          if (!mbar_wait_bounded(&kv_full[nks], nku & 1u, abort_flag, p.status,
+          if (j >= n_t[t]) continue;
+          if (!mbar_wait_bounded(&p_ready[t], static_cast<uint32_t>(j & 1), abort_flag, p.status,
                                  kWaitLimitNs)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          for (int t = 0; t < 2; ++t) {
-            if (j + 1 < n_t[t]) {
-              // P_t(j) lives in the S_t columns: wait until its GEMM is done.
-              if (!mbar_wait_bounded(&pv_done[t], static_cast<uint32_t>(j & 1), abort_flag,
-                                     p.status, kWaitLimitNs)) {
+          issue_PV(t, vs, j > 0);
+          mma_commit(&pv_done[t]);
+          if (j + 1 < n_t[t]) {
+            if (!k_next) {
+              if (!mbar_wait_bounded(&kv_full[nks], nku & 1u, abort_flag, p.status,
+                                     kWaitLimitNs)) {
                 ok = false;
                 break;
               }
-              issue_S(t, nks);
-              mma_commit(&s_full[t]);
+              k_next = true;
             }
+            if (!mbar_wait_bounded(&pv_done[t], static_cast<uint32_t>(j & 1), abort_flag,
+                                   p.status, kWaitLimitNs)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_S(t, nks);
+            mma_commit(&s_full[t]);
           }
+        }
+        if (!ok) break;
+        mma_commit(&kv_empty[vs]);  // V_j is free once the P·V GEMMs finish
+        if (j + 1 < nmax) {
+          if (!k_next &&
+              !mbar_wait_bounded(&kv_full[nks], nku & 1u, abort_flag, p.status, kWaitLimitNs)) {
+            ok = false;
+            break;
+          }
+          mma_commit(&kv_empty[nks]);  // K_{j+1} is free once its S GEMMs finish
         }
       }
       // Drain every MMA this thread issued before TMEM is released.
