@@ -49,6 +49,7 @@ struct FwdParams {
   int32_t* status;
   int Hq, group, Nq, Nk;
   int num_pairs;             // ceil(Nq / 256)
+  int num_bh;                // B * Hq
   float scale_log2;          // scale * log2(e) (* q/k descales for e4m3)
   float o_scale;             // v descale for e4m3, else 1
   int out_f32;               // 1: O is fp32, 0: O is bf16
@@ -68,7 +69,14 @@ struct FwdCfg {
   static constexpr uint32_t kFmt = FP8 ? 0u : 1u;       // e4m3 : bf16
   static constexpr int kKind = FP8 ? 1 : 0;
   static constexpr int kPCols = 128 * kEB / 4;          // TMEM columns holding P
-  static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1;
+  // Of every 8 exponentials per row, how many use ex2_poly (FMA pipe)
+  // instead of ex2.approx (MUFU); ATTN_EXP_EMU overrides it for tuning builds.
+#ifdef ATTN_EXP_EMU
+  static constexpr int kEmu = ATTN_EXP_EMU;
+#else
+  static constexpr int kEmu = 0;  // measured best on B200 (the MUFU is not the bound)
+#endif
+  static constexpr int kNumBars = 2 + 2 * kStages + 2 + 2 + 2 + 2 + 1;
   static constexpr size_t kSmemBytes =
       1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes + kNumBars * 8 + 16;
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
@@ -94,6 +102,62 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
   mbar_wait_bounded(bar, parity, &never, status, kWaitLimitNs);
 }
 
+// Work list.  One work item = two 128-row Q tiles (a "pair") of one
+// (batch, q-head) slice.  Causal items are ordered heaviest first (pair index
+// descending, then slice) — longest-processing-time order; non-causal items
+// slice-major so CTAs running at the same time share one slice's K/V in L2.
+// The persistent CTAs take items in a snake: round r gives CTA c item
+// r·G + c (r even) or r·G + G-1-c (r odd), which balances the decreasing
+// causal weights across CTAs.
+struct Item {
+  int bh, pair;
+};
+
+template <bool CAUSAL>
+__device__ __forceinline__ int item_index(int round, int cta, int G, int W) {
+  const int w = round * G + ((round & 1) ? (G - 1 - cta) : cta);
+  return w < W ? w : -1;
+}
+
+template <bool CAUSAL>
+__device__ __forceinline__ Item decode_item(int w, int num_bh, int num_pairs) {
+  Item it;
+  if (CAUSAL) {
+#if defined(ATTN_CAUSAL_CHUNK)
+    const int per = ATTN_CAUSAL_CHUNK * num_pairs;
+    const int ch = w / per, r = w - ch * per;
+    const int width = min(ATTN_CAUSAL_CHUNK, num_bh - ch * ATTN_CAUSAL_CHUNK);
+    it.pair = num_pairs - 1 - r / width;
+    it.bh = ch * ATTN_CAUSAL_CHUNK + r % width;
+#else
+    it.pair = num_pairs - 1 - w / num_bh;
+    it.bh = w % num_bh;
+#endif
+  } else {
+    it.bh = w / num_pairs;
+    it.pair = w % num_pairs;
+  }
+  return it;
+}
+
+// KV tiles (of 128 keys) each of the two Q tiles of `pair` needs.
+template <bool CAUSAL>
+__device__ __forceinline__ void kv_counts(int pair, int Nq, int Nk, int (&n_t)[2]) {
+  const int nkv_all = cdiv(Nk, 128);
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int qs = pair * 256 + 128 * t;
+    if (qs >= Nq) {
+      n_t[t] = 0;
+    } else if (CAUSAL) {
+      const int last_row = min(qs + 127, Nq - 1);
+      n_t[t] = min(nkv_all, last_row / 128 + 1);
+    } else {
+      n_t[t] = nkv_all;
+    }
+  }
+}
+
 template <int D, bool CAUSAL, bool FP8>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -107,43 +171,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sKV = smem + 2 * C::kTileBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + C::kStages * C::kTileBytes);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;
   uint64_t* kv_empty = kv_full + C::kStages;
   uint64_t* s_full = kv_empty + C::kStages;
   uint64_t* p_ready = s_full + 2;
   uint64_t* pv_done = p_ready + 2;
-  uint64_t* drain = pv_done + 2;
+  uint64_t* o_free = pv_done + 2;
+  uint64_t* drain = o_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;  // flat (batch, q-head)
-  const int b = bh / p.Hq;
-  const int h = bh - b * p.Hq;
-  const int hk = h / p.group;
-  // Causal: heaviest Q tiles first (longest-processing-time order).
-  const int pair = CAUSAL ? (p.num_pairs - 1 - static_cast<int>(blockIdx.y))
-                          : static_cast<int>(blockIdx.y);
-  const int q0 = pair * 256;
-  const int nkv_all = cdiv(p.Nk, 128);
-  int n_t[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int qs = q0 + 128 * t;
-    if (qs >= p.Nq) {
-      n_t[t] = 0;
-    } else if (CAUSAL) {
-      const int last_row = min(qs + 127, p.Nq - 1);
-      n_t[t] = min(nkv_all, last_row / 128 + 1);
-    } else {
-      n_t[t] = nkv_all;
-    }
-  }
-  const int nmax = max(n_t[0], n_t[1]);
+  const int G = static_cast<int>(gridDim.x);
+  const int cta = static_cast<int>(blockIdx.x);
+  const int W = p.num_bh * p.num_pairs;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -152,6 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&p_ready[t], 128);
       mbar_init(&pv_done[t], 1);
+      mbar_init(&o_free[t], 128);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -173,38 +221,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      mbar_arrive_expect_tx(q_full, 2 * C::kTileBytes);
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int c = 0; c < C::kNBox; ++c)
-          tma_load_4d(sQ + t * C::kTileBytes + c * C::kBoxBytes, &tmQ, q_full, c * C::kBoxCols,
-                      q0 + 128 * t, h, b);
-      int it = 0;
+      int ring = 0;  // K/V tiles issued so far (ring position)
+      int qi = 0;    // Q pairs issued so far
       bool ok = true;
-      for (int j = 0; j < nmax && ok; ++j) {
+      for (int r = 0; ok; ++r) {
+        const int w = item_index<CAUSAL>(r, cta, G, W);
+        if (w < 0) break;
+        const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
+        const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq, hk = h / p.group;
+        int n_t[2];
+        kv_counts<CAUSAL>(itm.pair, p.Nq, p.Nk, n_t);
+        const int nmax = max(n_t[0], n_t[1]);
+        // Q buffer: free once the previous pair's last S GEMMs completed.
+        if (!mbar_wait_bounded(q_empty, (static_cast<uint32_t>(qi) & 1u) ^ 1u, abort_flag,
+                               p.status, kWaitLimitNs)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(q_full, 2 * C::kTileBytes);
 #pragma unroll
-        for (int kv = 0; kv < 2; ++kv) {
-          const int s = it % C::kStages;
-          const uint32_t u = static_cast<uint32_t>(it / C::kStages);
-          if (!mbar_wait_bounded(&kv_empty[s], (u & 1u) ^ 1u, abort_flag, p.status,
-                                 kWaitLimitNs)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&kv_full[s], C::kTileBytes);
+        for (int t = 0; t < 2; ++t)
 #pragma unroll
           for (int c = 0; c < C::kNBox; ++c)
-            tma_load_4d(sKV + s * C::kTileBytes + c * C::kBoxBytes, kv ? &tmV : &tmK,
-                        &kv_full[s], c * C::kBoxCols, j * 128, hk, b);
-          ++it;
+            tma_load_4d(sQ + t * C::kTileBytes + c * C::kBoxBytes, &tmQ, q_full,
+                        c * C::kBoxCols, itm.pair * 256 + 128 * t, h, b);
+        ++qi;
+        for (int j = 0; j < nmax && ok; ++j) {
+#pragma unroll
+          for (int kv = 0; kv < 2; ++kv) {
+            const int s = ring % C::kStages;
+            const uint32_t u = static_cast<uint32_t>(ring / C::kStages);
+            if (!mbar_wait_bounded(&kv_empty[s], (u & 1u) ^ 1u, abort_flag, p.status,
+                                   kWaitLimitNs)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&kv_full[s], C::kTileBytes);
+#pragma unroll
+            for (int c = 0; c < C::kNBox; ++c)
+              tma_load_4d(sKV + s * C::kTileBytes + c * C::kBoxBytes, kv ? &tmV : &tmK,
+                          &kv_full[s], c * C::kBoxCols, j * 128, hk, b);
+            ++ring;
+          }
         }
       }
       // Wait for every copy this thread started before the CTA may exit.
-      drain_wait(q_full, 0, p.status);
+      if (qi > 0) drain_wait(q_full, static_cast<uint32_t>((qi - 1) & 1), p.status);
       for (int s = 0; s < C::kStages; ++s) {
-        if (it > s) {
-          const int armed = (it - 1 - s) / C::kStages + 1;
+        if (ring > s) {
+          const int armed = (ring - 1 - s) / C::kStages + 1;
           drain_wait(&kv_full[s], static_cast<uint32_t>((armed - 1) & 1), p.status);
         }
       }
@@ -236,71 +301,105 @@ __global__ void __launch_bounds__(kThreads, 1)
                            (acc || kk > 0) ? 1u : 0u);
         }
       };
-      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, p.status, kWaitLimitNs) &&
-                mbar_wait_bounded(&kv_full[0], 0, abort_flag, p.status, kWaitLimitNs);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < 2; ++t)
-          if (n_t[t] > 0) {
-            issue_S(t, 0);
-            mma_commit(&s_full[t]);
-          }
-        mma_commit(&kv_empty[0]);  // K_0 is free once both S GEMMs finish
-      }
-      // Per KV step j, for each Q tile t in turn: O_t += P_t(j)·V_j, then
-      // S_t(j+1) = Q_t·K_{j+1}ᵀ as soon as that P·V GEMM has finished reading
-      // P_t(j) (P lives in the S_t columns).  Tile t's next softmax can then
-      // start while the tensor cores run the other tile's GEMMs, so the two
-      // softmax warpgroups alternate with the tensor pipe.
-      for (int j = 0; j < nmax && ok; ++j) {
-        const int vs = (2 * j + 1) % C::kStages;
-        const uint32_t vu = static_cast<uint32_t>((2 * j + 1) / C::kStages);
-        const int nks = (2 * j + 2) % C::kStages;
-        const uint32_t nku = static_cast<uint32_t>((2 * j + 2) / C::kStages);
-        bool k_next = false;
-        if (!mbar_wait_bounded(&kv_full[vs], vu & 1u, abort_flag, p.status, kWaitLimitNs)) {
+      auto wait = [&](uint64_t* bar, int phase) {
+        return mbar_wait_bounded(bar, static_cast<uint32_t>(phase & 1), abort_flag, p.status,
+                                 kWaitLimitNs);
+      };
+      int ring = 0;                // ring position of this pair's K_0
+      int qi = 0;                  // pairs started
+      int pv_cnt[2] = {0, 0};      // P·V GEMMs committed per tile (pv_done phases)
+      int p_cnt[2] = {0, 0};       // p_ready phases consumed per tile
+      int items_t[2] = {0, 0};     // pairs in which tile t was active
+      bool ok = true;
+      for (int r = 0; ok; ++r) {
+        const int w = item_index<CAUSAL>(r, cta, G, W);
+        if (w < 0) break;
+        const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
+        int n_t[2];
+        kv_counts<CAUSAL>(itm.pair, p.Nq, p.Nk, n_t);
+        const int nmax = max(n_t[0], n_t[1]);
+        auto kst = [&](int j) { return (ring + 2 * j) % C::kStages; };
+        auto kph = [&](int j) { return (ring + 2 * j) / C::kStages; };
+        auto vst = [&](int j) { return (ring + 2 * j + 1) % C::kStages; };
+        auto vph = [&](int j) { return (ring + 2 * j + 1) / C::kStages; };
+        if (!wait(q_full, qi) || !wait(&kv_full[kst(0)], kph(0))) {
           ok = false;
           break;
         }
+        tc_fence_after();
         for (int t = 0; t < 2 && ok; ++t) {
-          if (j >= n_t[t]) continue;
-          if (!mbar_wait_bounded(&p_ready[t], static_cast<uint32_t>(j & 1), abort_flag, p.status,
-                                 kWaitLimitNs)) {
+          if (n_t[t] == 0) continue;
+          // S_t's columns hold the previous pair's last P_t until its P·V
+          // GEMM has completed.
+          if (pv_cnt[t] > 0 && !wait(&pv_done[t], pv_cnt[t] - 1)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          issue_PV(t, vs, j > 0);
-          mma_commit(&pv_done[t]);
-          if (j + 1 < n_t[t]) {
-            if (!k_next) {
-              if (!mbar_wait_bounded(&kv_full[nks], nku & 1u, abort_flag, p.status,
-                                     kWaitLimitNs)) {
-                ok = false;
-                break;
-              }
-              k_next = true;
+          issue_S(t, kst(0));
+          mma_commit(&s_full[t]);
+        }
+        if (!ok) break;
+        mma_commit(&kv_empty[kst(0)]);        // K_0 free once both S GEMMs finish
+        if (nmax == 1) mma_commit(q_empty);  // every S GEMM of this pair is issued
+        // Per KV step j, for each Q tile t in turn: O_t += P_t(j)·V_j, then
+        // S_t(j+1) = Q_t·K_{j+1}ᵀ as soon as that P·V GEMM has finished
+        // reading P_t(j) (P lives in the S_t columns).  Tile t's next
+        // softmax then overlaps the other tile's GEMMs.
+        for (int j = 0; j < nmax && ok; ++j) {
+          bool k_next = false;
+          if (!wait(&kv_full[vst(j)], vph(j))) {
+            ok = false;
+            break;
+          }
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= n_t[t]) continue;
+            if (!wait(&p_ready[t], p_cnt[t])) {
+              ok = false;
+              break;
             }
-            if (!mbar_wait_bounded(&pv_done[t], static_cast<uint32_t>(j & 1), abort_flag,
-                                   p.status, kWaitLimitNs)) {
+            ++p_cnt[t];
+            // The first P·V GEMM of a pair overwrites O_t: the previous pair's
+            // epilogue must have read it.
+            if (j == 0 && items_t[t] > 0 && !wait(&o_free[t], items_t[t] - 1)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_S(t, nks);
-            mma_commit(&s_full[t]);
+            issue_PV(t, vst(j), j > 0);
+            mma_commit(&pv_done[t]);
+            ++pv_cnt[t];
+            if (j + 1 < n_t[t]) {
+              if (!k_next) {
+                if (!wait(&kv_full[kst(j + 1)], kph(j + 1))) {
+                  ok = false;
+                  break;
+                }
+                k_next = true;
+              }
+              if (!wait(&pv_done[t], pv_cnt[t] - 1)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_S(t, kst(j + 1));
+              mma_commit(&s_full[t]);
+            }
+          }
+          if (!ok) break;
+          mma_commit(&kv_empty[vst(j)]);  // V_j free once the P·V GEMMs finish
+          if (j + 1 < nmax) {
+            if (!k_next && !wait(&kv_full[kst(j + 1)], kph(j + 1))) {
+              ok = false;
+              break;
+            }
+            mma_commit(&kv_empty[kst(j + 1)]);  // K_{j+1} free once its S GEMMs finish
+            if (j + 2 == nmax) mma_commit(q_empty);
           }
         }
-        if (!ok) break;
-        mma_commit(&kv_empty[vs]);  // V_j is free once the P·V GEMMs finish
-        if (j + 1 < nmax) {
-          if (!k_next &&
-              !mbar_wait_bounded(&kv_full[nks], nku & 1u, abort_flag, p.status, kWaitLimitNs)) {
-            ok = false;
-            break;
-          }
-          mma_commit(&kv_empty[nks]);  // K_{j+1} is free once its S GEMMs finish
-        }
+        for (int t = 0; t < 2; ++t)
+          if (n_t[t] > 0) ++items_t[t];
+        ring += 2 * nmax;
+        ++qi;
       }
       // Drain every MMA this thread issued before TMEM is released.
       mma_commit(drain);
@@ -315,117 +414,135 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_off + t * 128;
     const uint32_t tO = tmem + lane_off + 256 + t * D;
-    const int qs = q0 + 128 * t;
-    const int row = qs + r;
-    const int n = n_t[t];
     const float sl2 = p.scale_log2;
     const bool pos = sl2 >= 0.f;
     const float mask_val = pos ? -INFINITY : INFINITY;
-    float m = -INFINITY;
-    float l = 0.f;
+    int steps = 0;  // S tiles consumed so far (s_full / pv_done phases)
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      if (!warp_wait(&s_full[t], static_cast<uint32_t>(j & 1), abort_flag, p.status)) {
+    for (int rr = 0; ok; ++rr) {
+      const int w = item_index<CAUSAL>(rr, cta, G, W);
+      if (w < 0) break;
+      const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
+      int n_t[2];
+      kv_counts<CAUSAL>(itm.pair, p.Nq, p.Nk, n_t);
+      const int n = n_t[t];
+      if (n == 0) continue;
+      const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq;
+      const int qs = itm.pair * 256 + 128 * t;
+      const int row = qs + r;
+      float m = -INFINITY;
+      float l = 0.f;
+      for (int j = 0; j < n; ++j, ++steps) {
+        if (!warp_wait(&s_full[t], static_cast<uint32_t>(steps & 1), abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float s[128];
+        {
+          uint32_t r0[32], r1[32], r2[32], r3[32];
+          tmem_ld32(tS + 0, r0);
+          tmem_ld32(tS + 32, r1);
+          tmem_ld32(tS + 64, r2);
+          tmem_ld32(tS + 96, r3);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            s[i] = __uint_as_float(r0[i]);
+            s[32 + i] = __uint_as_float(r1[i]);
+            s[64 + i] = __uint_as_float(r2[i]);
+            s[96 + i] = __uint_as_float(r3[i]);
+          }
+        }
+        const int kbase = j * 128;
+        const bool edge = (kbase + 128 > p.Nk) || (CAUSAL && kbase + 127 > qs);
+        if (edge) {
+          const int lim = CAUSAL ? min(row + 1, p.Nk) : p.Nk;  // keys < lim are visible
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (kbase + c >= lim) s[c] = mask_val;
+        }
+        float red;
+        if (pos) {
+          float a0 = fmaxf(s[0], s[1]), a1 = fmaxf(s[2], s[3]);
+          float a2 = fmaxf(s[4], s[5]), a3 = fmaxf(s[6], s[7]);
+#pragma unroll
+          for (int c = 8; c < 128; c += 8) {
+            a0 = fmaxf(a0, fmaxf(s[c], s[c + 1]));
+            a1 = fmaxf(a1, fmaxf(s[c + 2], s[c + 3]));
+            a2 = fmaxf(a2, fmaxf(s[c + 4], s[c + 5]));
+            a3 = fmaxf(a3, fmaxf(s[c + 6], s[c + 7]));
+          }
+          red = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+        } else {
+          float a0 = fminf(s[0], s[1]), a1 = fminf(s[2], s[3]);
+          float a2 = fminf(s[4], s[5]), a3 = fminf(s[6], s[7]);
+#pragma unroll
+          for (int c = 8; c < 128; c += 8) {
+            a0 = fminf(a0, fminf(s[c], s[c + 1]));
+            a1 = fminf(a1, fminf(s[c + 2], s[c + 3]));
+            a2 = fminf(a2, fminf(s[c + 4], s[c + 5]));
+            a3 = fminf(a3, fminf(s[c + 6], s[c + 7]));
+          }
+          red = fminf(fminf(a0, a1), fminf(a2, a3));
+        }
+        const float m_cand = red * sl2;
+        float alpha = 1.f;
+        if (m_cand > m + 8.f) {  // m = -inf: any finite candidate moves it
+          alpha = ex2(m - m_cand);
+          m = m_cand;
+        }
+        const float neg_m = (m == -INFINITY) ? 0.f : -m;
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const float x = fmaf(s[c], sl2, neg_m);
+          s[c] = ((c & 7) < C::kEmu) ? ex2_poly(x) : ex2(x);
+        }
+        if constexpr (!FP8) {
+          uint32_t pk[64];
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            sum0 += s[2 * c];
+            sum1 += s[2 * c + 1];
+            pk[c] = pack_bf16(s[2 * c], s[2 * c + 1]);
+          }
+          tmem_st32(tS + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+          tmem_st32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+        } else {
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            sum0 += s[4 * c] + s[4 * c + 2];
+            sum1 += s[4 * c + 1] + s[4 * c + 3];
+            pk[c] = pack_e4m3x4(s[4 * c], s[4 * c + 1], s[4 * c + 2], s[4 * c + 3]);
+          }
+          tmem_st32(tS + 0, pk);
+        }
+        l = l * alpha + (sum0 + sum1);
+        const bool need = (j > 0) && (alpha != 1.f);
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + c * 32, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_ready[t]);
+      }
+      if (!ok) break;
+      // -------------------------------------------------------- epilogue
+      if (!warp_wait(&pv_done[t], static_cast<uint32_t>((steps - 1) & 1), abort_flag,
+                     p.status)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      float s[128];
-      {
-        uint32_t r0[32], r1[32], r2[32], r3[32];
-        tmem_ld32(tS + 0, r0);
-        tmem_ld32(tS + 32, r1);
-        tmem_ld32(tS + 64, r2);
-        tmem_ld32(tS + 96, r3);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          s[i] = __uint_as_float(r0[i]);
-          s[32 + i] = __uint_as_float(r1[i]);
-          s[64 + i] = __uint_as_float(r2[i]);
-          s[96 + i] = __uint_as_float(r3[i]);
-        }
-      }
-      const int kbase = j * 128;
-      const bool edge = (kbase + 128 > p.Nk) || (CAUSAL && kbase + 127 > qs);
-      if (edge) {
-        const int lim = CAUSAL ? min(row + 1, p.Nk) : p.Nk;  // keys < lim are visible
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (kbase + c >= lim) s[c] = mask_val;
-      }
-      float red;
-      if (pos) {
-        float a0 = fmaxf(s[0], s[1]), a1 = fmaxf(s[2], s[3]);
-#pragma unroll
-        for (int c = 4; c < 128; c += 4) {
-          a0 = fmaxf(a0, fmaxf(s[c], s[c + 1]));
-          a1 = fmaxf(a1, fmaxf(s[c + 2], s[c + 3]));
-        }
-        red = fmaxf(a0, a1);
-      } else {
-        float a0 = fminf(s[0], s[1]), a1 = fminf(s[2], s[3]);
-#pragma unroll
-        for (int c = 4; c < 128; c += 4) {
-          a0 = fminf(a0, fminf(s[c], s[c + 1]));
-          a1 = fminf(a1, fminf(s[c + 2], s[c + 3]));
-        }
-        red = fminf(a0, a1);
-      }
-      const float m_cand = red * sl2;
-      float alpha = 1.f;
-      if (m_cand > m + 8.f) {  // m = -inf: any finite candidate moves it
-        alpha = ex2(m - m_cand);
-        m = m_cand;
-      }
-      const float neg_m = (m == -INFINITY) ? 0.f : -m;
-      float sum0 = 0.f, sum1 = 0.f;
-      if constexpr (!FP8) {
-        uint32_t pk[64];
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float p0 = ex2(fmaf(s[2 * c], sl2, neg_m));
-          const float p1 = ex2(fmaf(s[2 * c + 1], sl2, neg_m));
-          sum0 += p0;
-          sum1 += p1;
-          pk[c] = pack_bf16(p0, p1);
-        }
-        tmem_st32(tS + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
-        tmem_st32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
-      } else {
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float p0 = ex2(fmaf(s[4 * c], sl2, neg_m));
-          const float p1 = ex2(fmaf(s[4 * c + 1], sl2, neg_m));
-          const float p2 = ex2(fmaf(s[4 * c + 2], sl2, neg_m));
-          const float p3 = ex2(fmaf(s[4 * c + 3], sl2, neg_m));
-          sum0 += p0 + p2;
-          sum1 += p1 + p3;
-          pk[c] = pack_e4m3x4(p0, p1, p2, p3);
-        }
-        tmem_st32(tS + 0, pk);
-      }
-      l = l * alpha + (sum0 + sum1);
-      const bool need = (j > 0) && (alpha != 1.f);
-      if (__any_sync(0xffffffffu, need)) {
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tO + c * 32, o);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_ready[t]);
-    }
-    // ---------------------------------------------------------- epilogue
-    if (ok && n > 0 && warp_wait(&pv_done[t], static_cast<uint32_t>((n - 1) & 1), abort_flag,
-                                 p.status)) {
       tc_fence_after();
       const float inv_l = p.o_scale / l;
       const int64_t obase = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
@@ -436,6 +553,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t o[32];
         tmem_ld32(tO + c * 32, o);
         tmem_wait_ld();
+        if (c == D / 32 - 1) {
+          // O_t has been read into registers: the next pair may overwrite it.
+          tc_fence_before();
+          mbar_arrive(&o_free[t]);
+        }
         if (live) {
           if (p.out_f32) {
             float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + obase + c * 32);
@@ -464,7 +586,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (live && p.lse)
-        p.lse[static_cast<int64_t>(bh) * p.Nq + row] = (m + __log2f(l)) * 0.69314718055994531f;
+        p.lse[static_cast<int64_t>(itm.bh) * p.Nq + row] =
+            (m + __log2f(l)) * 0.69314718055994531f;
     }
   }
 

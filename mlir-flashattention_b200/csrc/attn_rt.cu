@@ -155,6 +155,23 @@ int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int eb,
   return ATTN_OK;
 }
 
+// Multiprocessor count of the current device (cached per device).
+int sm_count(int* out) {
+  static std::atomic<int> cache[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(ATTN_ERR_INVALID, "bad device %d", dev);
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    cache[dev].store(n, std::memory_order_relaxed);
+  }
+  *out = n;
+  return ATTN_OK;
+}
+
 // -------------------------------------------------------------- launches
 template <int D, bool CAUSAL, bool FP8>
 int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
@@ -199,7 +216,13 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
   p.scale_log2 = sl2;
   p.o_scale = FP8 ? d.v_descale : 1.f;
   p.out_f32 = d.out_dtype == ATTN_F32 ? 1 : 0;
-  dim3 grid(static_cast<unsigned>(d.B * d.Hq), static_cast<unsigned>(p.num_pairs));
+  p.num_bh = static_cast<int>(d.B * d.Hq);
+  // Persistent launch: one CTA per SM (TMEM and shared memory allow one),
+  // each walking its share of the (slice, Q-tile pair) work list.
+  int sms = 0;
+  if ((rc = sm_count(&sms)) != ATTN_OK) return rc;
+  const int64_t items = static_cast<int64_t>(p.num_bh) * p.num_pairs;
+  dim3 grid(static_cast<unsigned>(std::min<int64_t>(items, sms)));
   kern<<<grid, attn_sm100::kThreads, C::kSmemBytes, stream>>>(mq, mk, mv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_sm100 launch");
