@@ -123,16 +123,8 @@ template <bool CAUSAL>
 __device__ __forceinline__ Item decode_item(int w, int num_bh, int num_pairs) {
   Item it;
   if (CAUSAL) {
-#if defined(ATTN_CAUSAL_CHUNK)
-    const int per = ATTN_CAUSAL_CHUNK * num_pairs;
-    const int ch = w / per, r = w - ch * per;
-    const int width = min(ATTN_CAUSAL_CHUNK, num_bh - ch * ATTN_CAUSAL_CHUNK);
-    it.pair = num_pairs - 1 - r / width;
-    it.bh = ch * ATTN_CAUSAL_CHUNK + r % width;
-#else
     it.pair = num_pairs - 1 - w / num_bh;
     it.bh = w % num_bh;
-#endif
   } else {
     it.bh = w / num_pairs;
     it.pair = w % num_pairs;
@@ -277,134 +269,137 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idS = make_idesc(128, 128, C::kFmt, false);
-      constexpr uint32_t idO = make_idesc(128, D, C::kFmt, true);
-      const uint32_t sQa = smem_u32(sQ);
-      const uint32_t sKVa = smem_u32(sKV);
-      auto issue_S = [&](int t, int stage) {
+    // The whole warp runs this schedule converged (waits by every lane, the
+    // MMA and commit instructions issued by one elected lane), so the
+    // descriptors below stay warp-uniform.
+    constexpr uint32_t idS = make_idesc(128, 128, C::kFmt, false);
+    constexpr uint32_t idO = make_idesc(128, D, C::kFmt, true);
+    // Descriptors of the first K step; later steps add (byte offset >> 4) to
+    // the 14-bit start-address field, which cannot carry (smem < 256 KB).
+    const uint64_t dQ0 = make_sdesc(smem_u32(sQ), 16, 1024);
+    const uint64_t dK0 = make_sdesc(smem_u32(sKV), 16, 1024);
+    const uint64_t dV0 = make_sdesc(smem_u32(sKV), C::kBoxBytes, 1024);
+    auto issue_S = [&](int t, int stage) {
+      const uint64_t a0 = dQ0 + static_cast<uint64_t>((t * C::kTileBytes) >> 4);
+      const uint64_t b0 = dK0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < C::kKStepsS; ++kk) {
-          const uint32_t kb = kk * 32;
-          const uint32_t off = (kb / 128) * C::kBoxBytes + (kb % 128);
-          const uint64_t a = make_sdesc(sQa + t * C::kTileBytes + off, 16, 1024);
-          const uint64_t bd = make_sdesc(sKVa + stage * C::kTileBytes + off, 16, 1024);
-          mma_ss<C::kKind>(tmem + t * 128, a, bd, idS, kk > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_PV = [&](int t, int stage, bool acc) {
+      for (int kk = 0; kk < C::kKStepsS; ++kk) {
+        constexpr int kBox = C::kBoxBytes;
+        const uint32_t off = ((kk * 32) / 128) * kBox + ((kk * 32) % 128);
+        mma_ss_warp<C::kKind>(tmem + t * 128, a0 + (off >> 4), b0 + (off >> 4), idS,
+                              kk > 0 ? 1u : 0u);
+      }
+    };
+    auto issue_PV = [&](int t, int stage, bool acc) {
+      const uint64_t b0 = dV0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < C::kKStepsPV; ++kk) {
-          const uint64_t bd = make_sdesc(
-              sKVa + stage * C::kTileBytes + kk * C::kKeysPerStep * 128, C::kBoxBytes, 1024);
-          mma_ts<C::kKind>(tmem + 256 + t * D, tmem + t * 128 + kk * 8, bd, idO,
-                           (acc || kk > 0) ? 1u : 0u);
-        }
-      };
-      auto wait = [&](uint64_t* bar, int phase) {
-        return mbar_wait_bounded(bar, static_cast<uint32_t>(phase & 1), abort_flag, p.status,
-                                 kWaitLimitNs);
-      };
-      int ring = 0;                // ring position of this pair's K_0
-      int qi = 0;                  // pairs started
-      int pv_cnt[2] = {0, 0};      // P·V GEMMs committed per tile (pv_done phases)
-      int p_cnt[2] = {0, 0};       // p_ready phases consumed per tile
-      int items_t[2] = {0, 0};     // pairs in which tile t was active
-      bool ok = true;
-      for (int r = 0; ok; ++r) {
-        const int w = item_index<CAUSAL>(r, cta, G, W);
-        if (w < 0) break;
-        const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
-        int n_t[2];
-        kv_counts<CAUSAL>(itm.pair, p.Nq, p.Nk, n_t);
-        const int nmax = max(n_t[0], n_t[1]);
-        auto kst = [&](int j) { return (ring + 2 * j) % C::kStages; };
-        auto kph = [&](int j) { return (ring + 2 * j) / C::kStages; };
-        auto vst = [&](int j) { return (ring + 2 * j + 1) % C::kStages; };
-        auto vph = [&](int j) { return (ring + 2 * j + 1) / C::kStages; };
-        if (!wait(q_full, qi) || !wait(&kv_full[kst(0)], kph(0))) {
+      for (int kk = 0; kk < C::kKStepsPV; ++kk)
+        mma_ts_warp<C::kKind>(tmem + 256 + t * D, tmem + t * 128 + kk * 8,
+                              b0 + static_cast<uint64_t>((kk * C::kKeysPerStep * 128) >> 4), idO,
+                              (acc || kk > 0) ? 1u : 0u);
+    };
+    auto wait = [&](uint64_t* bar, int phase) {
+      return warp_wait(bar, static_cast<uint32_t>(phase & 1), abort_flag, p.status);
+    };
+    int ring = 0;             // ring position of this pair's K_0
+    int qi = 0;               // pairs started
+    int pv_cnt[2] = {0, 0};   // P·V GEMMs committed per tile (pv_done phases)
+    int p_cnt[2] = {0, 0};    // p_ready phases consumed per tile
+    int items_t[2] = {0, 0};  // pairs in which tile t was active
+    bool ok = true;
+    for (int r = 0; ok; ++r) {
+      const int w = item_index<CAUSAL>(r, cta, G, W);
+      if (w < 0) break;
+      const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
+      int n_t[2];
+      kv_counts<CAUSAL>(itm.pair, p.Nq, p.Nk, n_t);
+      const int nmax = max(n_t[0], n_t[1]);
+      auto kst = [&](int j) { return (ring + 2 * j) % C::kStages; };
+      auto kph = [&](int j) { return (ring + 2 * j) / C::kStages; };
+      auto vst = [&](int j) { return (ring + 2 * j + 1) % C::kStages; };
+      auto vph = [&](int j) { return (ring + 2 * j + 1) / C::kStages; };
+      if (!wait(q_full, qi) || !wait(&kv_full[kst(0)], kph(0))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      for (int t = 0; t < 2 && ok; ++t) {
+        if (n_t[t] == 0) continue;
+        // S_t's columns hold the previous pair's last P_t until its P·V GEMM
+        // has completed.
+        if (pv_cnt[t] > 0 && !wait(&pv_done[t], pv_cnt[t] - 1)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (n_t[t] == 0) continue;
-          // S_t's columns hold the previous pair's last P_t until its P·V
-          // GEMM has completed.
-          if (pv_cnt[t] > 0 && !wait(&pv_done[t], pv_cnt[t] - 1)) {
-            ok = false;
-            break;
-          }
-          issue_S(t, kst(0));
-          mma_commit(&s_full[t]);
+        issue_S(t, kst(0));
+        mma_commit_warp(&s_full[t]);
+      }
+      if (!ok) break;
+      mma_commit_warp(&kv_empty[kst(0)]);        // K_0 free once both S GEMMs finish
+      if (nmax == 1) mma_commit_warp(q_empty);  // every S GEMM of this pair is issued
+      // Per KV step j, for each Q tile t in turn: O_t += P_t(j)·V_j, then
+      // S_t(j+1) = Q_t·K_{j+1}ᵀ as soon as that P·V GEMM has finished reading
+      // P_t(j) (P lives in the S_t columns).  Tile t's next softmax then
+      // overlaps the other tile's GEMMs.
+      for (int j = 0; j < nmax && ok; ++j) {
+        bool k_next = false;
+        if (!wait(&kv_full[vst(j)], vph(j))) {
+          ok = false;
+          break;
         }
-        if (!ok) break;
-        mma_commit(&kv_empty[kst(0)]);        // K_0 free once both S GEMMs finish
-        if (nmax == 1) mma_commit(q_empty);  // every S GEMM of this pair is issued
-        // Per KV step j, for each Q tile t in turn: O_t += P_t(j)·V_j, then
-        // S_t(j+1) = Q_t·K_{j+1}ᵀ as soon as that P·V GEMM has finished
-        // reading P_t(j) (P lives in the S_t columns).  Tile t's next
-        // softmax then overlaps the other tile's GEMMs.
-        for (int j = 0; j < nmax && ok; ++j) {
-          bool k_next = false;
-          if (!wait(&kv_full[vst(j)], vph(j))) {
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= n_t[t]) continue;
+          if (!wait(&p_ready[t], p_cnt[t])) {
             ok = false;
             break;
           }
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (j >= n_t[t]) continue;
-            if (!wait(&p_ready[t], p_cnt[t])) {
-              ok = false;
-              break;
+          ++p_cnt[t];
+          // The first P·V GEMM of a pair overwrites O_t: the previous pair's
+          // epilogue must have read it.
+          if (j == 0 && items_t[t] > 0 && !wait(&o_free[t], items_t[t] - 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_PV(t, vst(j), j > 0);
+          mma_commit_warp(&pv_done[t]);
+          ++pv_cnt[t];
+          if (j + 1 < n_t[t]) {
+            if (!k_next) {
+              if (!wait(&kv_full[kst(j + 1)], kph(j + 1))) {
+                ok = false;
+                break;
+              }
+              k_next = true;
             }
-            ++p_cnt[t];
-            // The first P·V GEMM of a pair overwrites O_t: the previous pair's
-            // epilogue must have read it.
-            if (j == 0 && items_t[t] > 0 && !wait(&o_free[t], items_t[t] - 1)) {
+            if (!wait(&pv_done[t], pv_cnt[t] - 1)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_PV(t, vst(j), j > 0);
-            mma_commit(&pv_done[t]);
-            ++pv_cnt[t];
-            if (j + 1 < n_t[t]) {
-              if (!k_next) {
-                if (!wait(&kv_full[kst(j + 1)], kph(j + 1))) {
-                  ok = false;
-                  break;
-                }
-                k_next = true;
-              }
-              if (!wait(&pv_done[t], pv_cnt[t] - 1)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              issue_S(t, kst(j + 1));
-              mma_commit(&s_full[t]);
-            }
-          }
-          if (!ok) break;
-          mma_commit(&kv_empty[vst(j)]);  // V_j free once the P·V GEMMs finish
-          if (j + 1 < nmax) {
-            if (!k_next && !wait(&kv_full[kst(j + 1)], kph(j + 1))) {
-              ok = false;
-              break;
-            }
-            mma_commit(&kv_empty[kst(j + 1)]);  // K_{j+1} free once its S GEMMs finish
-            if (j + 2 == nmax) mma_commit(q_empty);
+            issue_S(t, kst(j + 1));
+            mma_commit_warp(&s_full[t]);
           }
         }
-        for (int t = 0; t < 2; ++t)
-          if (n_t[t] > 0) ++items_t[t];
-        ring += 2 * nmax;
-        ++qi;
+        if (!ok) break;
+        mma_commit_warp(&kv_empty[vst(j)]);  // V_j free once the P·V GEMMs finish
+        if (j + 1 < nmax) {
+          if (!k_next && !wait(&kv_full[kst(j + 1)], kph(j + 1))) {
+            ok = false;
+            break;
+          }
+          mma_commit_warp(&kv_empty[kst(j + 1)]);  // K_{j+1} free once its S GEMMs finish
+          if (j + 2 == nmax) mma_commit_warp(q_empty);
+        }
       }
-      // Drain every MMA this thread issued before TMEM is released.
-      mma_commit(drain);
-      drain_wait(drain, 0, p.status);
+      for (int t = 0; t < 2; ++t)
+        if (n_t[t] > 0) ++items_t[t];
+      ring += 2 * nmax;
+      ++qi;
     }
+    // Drain every MMA this warp issued before TMEM is released.
+    mma_commit_warp(drain);
+    if (lane == 0) drain_wait(drain, 0, p.status);
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
