@@ -69,13 +69,6 @@ struct FwdCfg {
   static constexpr uint32_t kFmt = FP8 ? 0u : 1u;       // e4m3 : bf16
   static constexpr int kKind = FP8 ? 1 : 0;
   static constexpr int kPCols = 128 * kEB / 4;          // TMEM columns holding P
-  // Of every 8 exponentials per row, how many use ex2_poly (FMA pipe)
-  // instead of ex2.approx (MUFU); ATTN_EXP_EMU overrides it for tuning builds.
-#ifdef ATTN_EXP_EMU
-  static constexpr int kEmu = ATTN_EXP_EMU;
-#else
-  static constexpr int kEmu = 0;  // measured best on B200 (the MUFU is not the bound)
-#endif
   static constexpr int kNumBars = 2 + 2 * kStages + 2 + 2 + 2 + 2 + 1;
   static constexpr size_t kSmemBytes =
       1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes + kNumBars * 8 + 16;
@@ -492,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 128; ++c) {
           const float x = fmaf(s[c], sl2, neg_m);
-          s[c] = ((c & 7) < C::kEmu) ? ex2_poly(x) : ex2(x);
+          s[c] = ex2(x);
         }
         if constexpr (!FP8) {
           uint32_t pk[64];

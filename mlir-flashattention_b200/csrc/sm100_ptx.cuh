@@ -311,27 +311,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA and integer pipes, for offloading part of the softmax
-// exponentials from the special-function unit.  Cody-Waite style range
-// reduction: x = j + f with j = round-to-nearest(x) (obtained by adding
-// 1.5·2^23, which leaves j in the low mantissa bits of t) and f in
-// [-0.5, 0.5]; 2^f from a cubic fitted here by iteratively reweighted least
-// squares for minimum maximum relative error (max relative error 7.5e-5 over
-// [-0.5, 0.5], below bf16's 2^-9 rounding); 2^j is added to the exponent
-// field: bits(t) << 23 == j << 23 (mod 2^32) because bits(1.5·2^23) has nine
-// trailing zero bits.  x is clamped to >= -126 so the result stays a positive
-// number (>= 2^-126.5) instead of wrapping; such values are below bf16/e4m3
-// resolution of any row sum they join.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float t = x + 12582912.0f;
-  const float f = x - (t - 12582912.0f);
-  float p = fmaf(0.05517166493030257f, f, 0.24261112187714973f);
-  p = fmaf(p, f, 0.6932609862225384f);
-  p = fmaf(p, f, 0.9999280735783092f);
-  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
-}
-
 // Pack two floats into bf16x2 with round-to-nearest-even; `lo` in bits 0..15.
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
