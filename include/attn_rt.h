@@ -161,6 +161,15 @@ ATTN_API int32_t _mlir_ciface_attn_fused_bf16_nomask_4d(AttnMemRef4D* Q, AttnMem
 ATTN_API int32_t _mlir_ciface_attn_fused_bf16_causal_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
                                                float scale, AttnMemRef4D* O, AttnMemRef4D* LSE);
 
+/* Rank-4 bf16 with a general i1 mask memref<BxHxNqxNkxi1> (one byte per
+ * element, 1 = masked; batch/head strides may be 0 to broadcast one mask);
+ * the reference op's `mask` operand (AttentionOps.td:40, TilingPass.cpp:254-277)
+ * on the tensor-core path. */
+ATTN_API int32_t _mlir_ciface_attn_fused_bf16_mask_4d(AttnMemRef4D* Q, AttnMemRef4D* K,
+                                                      AttnMemRef4D* V, float scale,
+                                                      AttnMemRef4D* mask, AttnMemRef4D* O,
+                                                      AttnMemRef4D* LSE);
+
 /* Rank-4 e4m3 in (per-tensor dequantisation factors) / bf16 out. */
 ATTN_API int32_t _mlir_ciface_attn_fused_e4m3_nomask_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
                                                float scale, float q_descale, float k_descale,

@@ -112,6 +112,8 @@ def lib():
             fn.restype, fn.argtypes = ctypes.c_int32, [m4, m4, m4, f, m4, m4]
             fn = getattr(L, f"_mlir_ciface_attn_fused_e4m3_{name}_4d")
             fn.restype, fn.argtypes = ctypes.c_int32, [m4, m4, m4, f, f, f, f, m4, m4]
+        L._mlir_ciface_attn_fused_bf16_mask_4d.restype = ctypes.c_int32
+        L._mlir_ciface_attn_fused_bf16_mask_4d.argtypes = [m4, m4, m4, f, m4, m4, m4]
         L._mlir_ciface_attn_fused_f32_mask.restype = ctypes.c_int32
         L._mlir_ciface_attn_fused_f32_mask.argtypes = [m2, m2, m2, f, m2, m2]
         _lib = L

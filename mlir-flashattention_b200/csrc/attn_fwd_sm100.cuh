@@ -53,7 +53,16 @@ struct FwdParams {
   float scale_log2;          // scale * log2(e) (* q/k descales for e4m3)
   float o_scale;             // v descale for e4m3, else 1
   int out_f32;               // 1: O is fp32, 0: O is bf16
+  // Dense i1 mask (one byte per element, 1 = masked), mode 2 only.
+  const uint8_t* mask;
+  int64_t m_sb, m_sh, m_sn;  // byte strides: batch, head, row (column stride 1)
+  int mask_vec;              // 1: rows 16-byte aligned (vector loads)
 };
+
+// Mask modes of the kernel (compile-time specialisations).
+constexpr int kMaskNone = 0;    // no mask operand
+constexpr int kMaskCausal = 1;  // mask[i][j] = j > i, computed
+constexpr int kMaskDense = 2;   // explicit i1 mask read from memory
 
 template <int D, bool FP8>
 struct FwdCfg {
@@ -143,11 +152,37 @@ __device__ __forceinline__ void kv_counts(int pair, int Nq, int Nk, int (&n_t)[2
   }
 }
 
-template <int D, bool CAUSAL, bool FP8>
+// 128 mask bytes of one row for keys [kbase, kbase+128): bit c of the
+// returned words is set when key kbase+c is masked or does not exist.
+__device__ __forceinline__ void load_mask_row(const uint8_t* mrow, int kbase, int Nk, bool vec,
+                                              uint32_t (&bits)[4]) {
+  bits[0] = bits[1] = bits[2] = bits[3] = 0u;
+  if (vec && kbase + 128 <= Nk) {
+    const uint4* src = reinterpret_cast<const uint4*>(mrow + kbase);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint4 v = __ldg(src + q);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb)
+          if ((w[e] >> (8 * bb)) & 0xFFu) bits[q / 2] |= 1u << ((q & 1) * 16 + e * 4 + bb);
+    }
+  } else {
+#pragma unroll 4
+    for (int c = 0; c < 128; ++c)
+      if (kbase + c >= Nk || mrow[kbase + c] != 0) bits[c >> 5] |= 1u << (c & 31);
+  }
+}
+
+template <int D, int MODE, bool FP8>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  constexpr bool CAUSAL = MODE == kMaskCausal;
+  constexpr bool DENSE = MODE == kMaskDense;
   using C = FwdCfg<D, FP8>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -420,7 +455,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = qs + r;
       float m = -INFINITY;
       float l = 0.f;
+      const uint8_t* mrow = nullptr;
+      if constexpr (DENSE)
+        mrow = p.mask + b * p.m_sb + h * p.m_sh + static_cast<int64_t>(min(row, p.Nq - 1)) * p.m_sn;
       for (int j = 0; j < n; ++j, ++steps) {
+        uint32_t mbits[4];
+        if constexpr (DENSE) load_mask_row(mrow, j * 128, p.Nk, p.mask_vec != 0, mbits);
         if (!warp_wait(&s_full[t], static_cast<uint32_t>(steps & 1), abort_flag, p.status)) {
           ok = false;
           break;
@@ -443,7 +483,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const int kbase = j * 128;
-        const bool edge = (kbase + 128 > p.Nk) || (CAUSAL && kbase + 127 > qs);
+        if constexpr (DENSE) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if ((mbits[c >> 5] >> (c & 31)) & 1u) s[c] = mask_val;
+        }
+        const bool edge = !DENSE && ((kbase + 128 > p.Nk) || (CAUSAL && kbase + 127 > qs));
         if (edge) {
           const int lim = CAUSAL ? min(row + 1, p.Nk) : p.Nk;  // keys < lim are visible
 #pragma unroll

@@ -173,10 +173,10 @@ int sm_count(int* out) {
 }
 
 // -------------------------------------------------------------- launches
-template <int D, bool CAUSAL, bool FP8>
+template <int D, int MODE, bool FP8>
 int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
   using C = attn_sm100::FwdCfg<D, FP8>;
-  auto kern = attn_sm100::attn_fwd_sm100_kernel<D, CAUSAL, FP8>;
+  auto kern = attn_sm100::attn_fwd_sm100_kernel<D, MODE, FP8>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -216,6 +216,17 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
   p.scale_log2 = sl2;
   p.o_scale = FP8 ? d.v_descale : 1.f;
   p.out_f32 = d.out_dtype == ATTN_F32 ? 1 : 0;
+  if (MODE == attn_sm100::kMaskDense) {
+    p.mask = d.mask;
+    p.m_sb = d.mask_stride[0];
+    p.m_sh = d.mask_stride[1];
+    p.m_sn = d.mask_stride[2];
+    const bool rows_aligned = (reinterpret_cast<uintptr_t>(d.mask) & 15u) == 0 &&
+                              (d.Nq == 1 || d.mask_stride[2] % 16 == 0) &&
+                              (d.Hq == 1 || d.mask_stride[1] % 16 == 0) &&
+                              (d.B == 1 || d.mask_stride[0] % 16 == 0);
+    p.mask_vec = rows_aligned ? 1 : 0;
+  }
   p.num_bh = static_cast<int>(d.B * d.Hq);
   // Persistent launch: one CTA per SM (TMEM and shared memory allow one),
   // each walking its share of the (slice, Q-tile pair) work list.
@@ -304,8 +315,6 @@ int validate(const AttnDesc& d) {
       if (d.dtype == ATTN_E4M3 && d.D != 128)
         return fail(ATTN_ERR_UNSUPPORTED, "e4m3 path supports head_dim 128 (got %lld)",
                     (long long)d.D);
-      if (d.mask_kind == ATTN_MASK_DENSE)
-        return fail(ATTN_ERR_UNSUPPORTED, "dense masks are supported on the f32 path only");
       if (d.dtype == ATTN_E4M3 && !(d.q_descale > 0.f && d.k_descale > 0.f && d.v_descale > 0.f))
         return fail(ATTN_ERR_INVALID, "e4m3 descales must be positive");
       if (!aligned16(d.q) || !aligned16(d.k) || !aligned16(d.v) || !aligned16(d.o))
@@ -322,21 +331,24 @@ int validate(const AttnDesc& d) {
   }
 }
 
+template <int D, bool FP8>
+int dispatch_mode(const AttnDesc& d, int32_t* status, cudaStream_t s) {
+  switch (d.mask_kind) {
+    case ATTN_MASK_CAUSAL: return launch_sm100<D, attn_sm100::kMaskCausal, FP8>(d, status, s);
+    case ATTN_MASK_DENSE: return launch_sm100<D, attn_sm100::kMaskDense, FP8>(d, status, s);
+    default: return launch_sm100<D, attn_sm100::kMaskNone, FP8>(d, status, s);
+  }
+}
+
 int dispatch(const AttnDesc& d, int32_t* status, cudaStream_t s) {
-  const bool causal = d.mask_kind == ATTN_MASK_CAUSAL;
   if (d.dtype == ATTN_F32) {
     if (d.D <= 64) return launch_f32<64>(d, s);
     if (d.D <= 128) return launch_f32<128>(d, s);
     return launch_f32<256>(d, s);
   }
-  if (d.dtype == ATTN_BF16) {
-    if (d.D == 64) return causal ? launch_sm100<64, true, false>(d, status, s)
-                                 : launch_sm100<64, false, false>(d, status, s);
-    return causal ? launch_sm100<128, true, false>(d, status, s)
-                  : launch_sm100<128, false, false>(d, status, s);
-  }
-  return causal ? launch_sm100<128, true, true>(d, status, s)
-                : launch_sm100<128, false, true>(d, status, s);
+  if (d.dtype == ATTN_BF16)
+    return d.D == 64 ? dispatch_mode<64, false>(d, status, s) : dispatch_mode<128, false>(d, status, s);
+  return dispatch_mode<128, true>(d, status, s);
 }
 
 // ------------------------------------------------- memref-descriptor layer
@@ -569,9 +581,11 @@ int run_views(int dtype, int out_dtype, int mask_kind, const View& Q, const View
     if (M->size[2] != Q.size[2] || M->size[3] != K.size[2])
       return fail(ATTN_ERR_SHAPE, "mask must be [seq_q, seq_k]");
     if (M->stride[3] != 1) return fail(ATTN_ERR_STRIDE, "mask columns must be unit-stride");
+    if ((M->size[0] != 1 && M->size[0] != Q.size[0]) || (M->size[1] != 1 && M->size[1] != Q.size[1]))
+      return fail(ATTN_ERR_SHAPE, "mask batch/head extents must be 1 or match Q");
     d.mask = reinterpret_cast<const uint8_t*>(M->ptr);
-    d.mask_stride[0] = M->stride[0];
-    d.mask_stride[1] = M->stride[1];
+    d.mask_stride[0] = M->size[0] == 1 ? 0 : M->stride[0];  // extent 1 broadcasts
+    d.mask_stride[1] = M->size[1] == 1 ? 0 : M->stride[1];
     d.mask_stride[2] = M->stride[2];
   }
   const bool dev_q = is_device_ptr(d.q);
@@ -724,6 +738,16 @@ F32_4D(_mlir_ciface_attn_fused_f32_causal_4d, ATTN_MASK_CAUSAL)
   }
 BF16_4D(_mlir_ciface_attn_fused_bf16_nomask_4d, ATTN_MASK_NONE)
 BF16_4D(_mlir_ciface_attn_fused_bf16_causal_4d, ATTN_MASK_CAUSAL)
+
+int32_t _mlir_ciface_attn_fused_bf16_mask_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
+                                             float scale, AttnMemRef4D* mask, AttnMemRef4D* O,
+                                             AttnMemRef4D* LSE) {
+  if (!Q || !K || !V || !O || !mask) return fail(ATTN_ERR_INVALID, "null memref descriptor");
+  View L, M = view4(mask, 1);
+  if (LSE) L = view4(LSE, 4);
+  return run_views(ATTN_BF16, ATTN_BF16, ATTN_MASK_DENSE, view4(Q, 2), view4(K, 2), view4(V, 2),
+                   view4(O, 2), scale, 1.f, 1.f, 1.f, LSE ? &L : nullptr, &M);
+}
 
 #define E4M3_4D(NAME, KIND)                                                                  \
   int32_t NAME(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V, float scale, float qd,     \

@@ -26,7 +26,7 @@
 //     (the causal generic), or a mask value carrying the unit attribute
 //     `attention.causal` on its defining op                -> "causal"
 //   * anything else                                      -> "mask" (dense i1
-//     operand, f32 only; other element types are rejected with an error)
+//     operand; rank-2 f32 or rank-4 bf16, others rejected with an error)
 //
 // The pass is stateless.  Unlike the reference's FuncOp-anchored passes
 // (AttentionPasses.td:14,27) it is anchored on the module, because it adds
@@ -133,8 +133,9 @@ struct FusedToRuntimeCall : public OpRewritePattern<FusedOp> {
     if (rank != 2 && rank != 4) return op.emitOpError("operands must be rank-2 or rank-4");
 
     MaskKind kind = classifyMask(op.getMask());
-    if (kind == MaskKind::Dense && (dt != "f32" || rank != 2))
-      return op.emitOpError("a general i1 mask is supported for rank-2 f32 operands only");
+    if (kind == MaskKind::Dense && !((dt == "f32" && rank == 2) || (dt == "bf16" && rank == 4)))
+      return op.emitOpError("a general i1 mask is supported for rank-2 f32 and rank-4 bf16 "
+                            "operands");
     if (dt != "f32" && rank != 4)
       return op.emitOpError("bf16/e4m3 operands are lowered in their rank-4 form");
 

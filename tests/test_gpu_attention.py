@@ -165,3 +165,69 @@ def test_unsupported_variants_raise(pkg):
     with pytest.raises(pkg.AttentionError) as e:
         pkg.fused(q, q, q, 0.1, output=o)
     assert e.value.code == -5
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_bf16_dense_mask_parity(pkg, wl, oracle, D):
+    """The op's general i1 mask on the tensor-core path (per-slice masks)."""
+    w = wl.Workload("t", "bf16", 2, 3, 3, 1000, D, False, seed=40 + D)
+    inp = wl.make_inputs(w)
+    rng = np.random.default_rng(D)
+    M = rng.random((2, 3, 1000, 1000)) < 0.35
+    M[..., 0] = False  # a row masked over a whole first tile is NaN in the reference
+    q, k, v = wl.to_device(inp, w)
+    L = torch.empty((2, 3, 1000), dtype=torch.float32, device="cuda")
+    out = pkg.fused(q, k, v, w.scale, mask=torch.from_numpy(M).cuda(), lse=L)
+    pkg.check_status(0)
+    ref, ref_lse = oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale, mask=M)
+    assert _rel(out.float().cpu().numpy(), ref) <= 2e-2
+    assert np.abs(L.cpu().numpy() - ref_lse).max() <= 1e-3
+
+
+def test_dense_causal_mask_equals_causal_variant(pkg, wl):
+    """A causal pattern given as an explicit i1 mask and run on the dense-mask
+    path (every KV tile visited) gives the same bits as the causal
+    specialisation, which skips the fully masked tiles: those tiles only add
+    exact zeros."""
+    import ctypes
+
+    w = wl.Workload("t", "bf16", 1, 4, 4, 640, 128, True, seed=8)
+    inp = wl.make_inputs(w)
+    q, k, v = wl.to_device(inp, w)
+    a = pkg.fused(q, k, v, w.scale, causal=True)
+    m8 = torch.ones(640, 640, dtype=torch.uint8, device="cuda").triu(1).expand(1, 4, 640, 640)
+    out = torch.empty_like(a)
+    d = pkg.AttnDesc()
+    d.dtype, d.out_dtype, d.mask_kind = pkg.ATTN_BF16, pkg.ATTN_BF16, pkg.MASK_DENSE
+    d.B, d.Hq, d.Hkv, d.Nq, d.Nk, d.D = 1, 4, 4, 640, 640, 128
+    for dst, t in ((d.q_stride, q), (d.k_stride, k), (d.v_stride, v), (d.o_stride, out)):
+        dst[0], dst[1], dst[2] = t.stride(0), t.stride(1), t.stride(2)
+    d.q, d.k, d.v, d.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+    d.mask = m8.data_ptr()
+    d.mask_stride[0], d.mask_stride[1], d.mask_stride[2] = m8.stride(0), m8.stride(1), m8.stride(2)
+    d.scale = w.scale
+    d.q_descale = d.k_descale = d.v_descale = 1.0
+    rc = pkg.lib().attn_fwd(ctypes.byref(d), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, pkg.last_error()
+    pkg.check_status(0)
+    assert torch.equal(out, a)
+
+
+def test_bf16_mask_memref_with_host_buffers(pkg, wl, oracle):
+    """_mlir_ciface_attn_fused_bf16_mask_4d on host memrefs, broadcast mask."""
+    w = wl.Workload("t", "bf16", 1, 2, 2, 300, 64, False, seed=12)
+    inp = wl.make_inputs(w)
+    rng = np.random.default_rng(3)
+    M = rng.random((300, 300)) < 0.5
+    M[:, 0] = False
+    q, k, v = (t.cpu() for t in wl.to_device(inp, w))
+    o = torch.empty_like(q)
+    m = torch.from_numpy(M.astype(np.uint8)).reshape(1, 1, 300, 300)
+    lse = torch.empty((0, 0, 0, 1), dtype=torch.float32)
+    rc = pkg.lib()._mlir_ciface_attn_fused_bf16_mask_4d(
+        pkg.memref(q), pkg.memref(k), pkg.memref(v), w.scale, pkg.memref(m), pkg.memref(o),
+        pkg.memref(lse))
+    assert rc == 0, pkg.last_error()
+    ref, _ = oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale,
+                                 mask=np.broadcast_to(M, (1, 2, 300, 300)))
+    assert _rel(o.float().numpy(), ref) <= 2e-2
