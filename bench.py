@@ -117,6 +117,15 @@ class ClockSampler:
                 "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
 
 
+def host_threads() -> int:
+    """Every host core this process may run on (torchrun sets OMP_NUM_THREADS
+    to 1 per process, so the oracle's thread count is passed explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_sample(w, budget_s=12.0, max_tiles=None):
     """Time the oracle on c. `budget_s` of q tiles of the workload (all host
     threads; one tile per thread per batch) and extrapolate to the workload.
@@ -129,7 +138,7 @@ def cpu_sample(w, budget_s=12.0, max_tiles=None):
     import __graft_entry__ as ge  # noqa: PLC0415
 
     o = ge.oracle()
-    cores = o.max_threads()
+    cores = host_threads()
     rng = np.random.Generator(np.random.PCG64(w.seed))
     # One (batch, head) slice of the workload's shape is enough: every slice
     # costs the same.
@@ -165,7 +174,7 @@ def reference_arm(args, w, world):
     import __graft_entry__ as ge  # noqa: PLC0415
 
     o = ge.oracle()
-    cores = o.max_threads()
+    cores = host_threads()
     rng = np.random.Generator(np.random.PCG64(w.seed))
     q = rng.standard_normal((1, 1, w.N, w.D), dtype=np.float32)
     k = rng.standard_normal((1, 1, w.N, w.D), dtype=np.float32)

@@ -103,6 +103,12 @@ ATTN_API int attn_rt_init(int device);
  * kernels of `device`; returns ATTN_OK or the first recorded ATTN_ERR_*. */
 ATTN_API int attn_rt_check_status(int device, void* stream);
 
+/* Failure-detection self-test (no counterpart in the reference): launches one
+ * CTA that waits, with the bounded mbarrier wait every kernel here uses, on a
+ * barrier nothing arrives on, giving up after `limit_ns` (<= 2 s).  Returns
+ * ATTN_ERR_TIMEOUT when the bound works; the device stays usable. */
+ATTN_API int attn_rt_probe_timeout(int64_t limit_ns);
+
 /* Human-readable name of a status code. */
 ATTN_API const char* attn_rt_status_string(int code);
 

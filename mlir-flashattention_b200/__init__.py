@@ -101,6 +101,8 @@ def lib():
         L.attn_rt_last_error.argtypes = []
         L.attn_rt_version.restype = ctypes.c_int
         L.attn_rt_launch_count.restype = ctypes.c_int64
+        L.attn_rt_probe_timeout.restype = ctypes.c_int
+        L.attn_rt_probe_timeout.argtypes = [ctypes.c_int64]
         m2, m4 = ctypes.POINTER(AttnMemRef2D), ctypes.POINTER(AttnMemRef4D)
         f = ctypes.c_float
         for name in ("nomask", "causal"):

@@ -280,6 +280,20 @@ int launch_f32(const AttnDesc& d, cudaStream_t stream) {
   return ATTN_OK;
 }
 
+// Failure-detection self-test: one CTA waits, with the bounded wait every
+// kernel here uses, on an mbarrier that nothing ever arrives on.
+__global__ void probe_timeout_kernel(uint64_t limit_ns, int32_t* status) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    attn_sm100::mbar_init(&bar, 1);
+    abort_flag = 0;
+    attn_sm100::fence_mbar_init();
+  }
+  __syncthreads();
+  attn_sm100::mbar_wait_bounded(&bar, 0, &abort_flag, status, limit_ns);
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int validate(const AttnDesc& d) {
@@ -673,6 +687,19 @@ const char* attn_rt_status_string(int code) {
 }
 
 int attn_rt_init(int device) { return init_device(device); }
+
+int attn_rt_probe_timeout(int64_t limit_ns) {
+  if (limit_ns <= 0 || limit_ns > 2000000000ll)
+    return fail(ATTN_ERR_INVALID, "probe limit must be in (0, 2 s]");
+  int dev = 0, rc;
+  if ((rc = current_device(&dev)) != ATTN_OK) return rc;
+  if ((rc = init_device(dev)) != ATTN_OK) return rc;
+  DevState& st = g_dev[dev];
+  probe_timeout_kernel<<<1, 32, 0, st.s_compute>>>(static_cast<uint64_t>(limit_ns), st.status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "probe launch");
+  return attn_rt_check_status(dev, st.s_compute);
+}
 
 int attn_rt_check_status(int device, void* stream) {
   int rc = init_device(device);

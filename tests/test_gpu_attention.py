@@ -231,3 +231,20 @@ def test_bf16_mask_memref_with_host_buffers(pkg, wl, oracle):
     ref, _ = oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale,
                                  mask=np.broadcast_to(M, (1, 2, 300, 300)))
     assert _rel(o.float().numpy(), ref) <= 2e-2
+
+
+def test_bounded_wait_times_out_and_device_stays_usable(pkg, wl, oracle):
+    """A wait on a barrier nothing arrives on gives up after its limit with
+    ATTN_ERR_TIMEOUT (no trap, no hang), and the next attention call is
+    correct."""
+    import time
+
+    t0 = time.perf_counter()
+    rc = pkg.lib().attn_rt_probe_timeout(20_000_000)  # 20 ms
+    assert rc == -7, pkg.last_error()
+    assert time.perf_counter() - t0 < 5.0
+    w = wl.Workload("t", "bf16", 1, 2, 2, 256, 128, True, seed=1)
+    inp = wl.make_inputs(w)
+    got, _ = _run_pkg(pkg, wl, w, inp, True)
+    ref, _ = _ref(oracle, inp, w, True)
+    assert _rel(got, ref) <= 2e-2
