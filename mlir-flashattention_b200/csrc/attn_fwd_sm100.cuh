@@ -497,27 +497,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         float red;
         if (pos) {
-          float a0 = fmaxf(s[0], s[1]), a1 = fmaxf(s[2], s[3]);
-          float a2 = fmaxf(s[4], s[5]), a3 = fmaxf(s[6], s[7]);
+          float a0 = max3(s[0], s[1], s[2]), a1 = max3(s[3], s[4], s[5]);
 #pragma unroll
-          for (int c = 8; c < 128; c += 8) {
-            a0 = fmaxf(a0, fmaxf(s[c], s[c + 1]));
-            a1 = fmaxf(a1, fmaxf(s[c + 2], s[c + 3]));
-            a2 = fmaxf(a2, fmaxf(s[c + 4], s[c + 5]));
-            a3 = fmaxf(a3, fmaxf(s[c + 6], s[c + 7]));
+          for (int c = 6; c < 126; c += 4) {
+            a0 = max3(a0, s[c], s[c + 1]);
+            a1 = max3(a1, s[c + 2], s[c + 3]);
           }
-          red = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+          red = max3(a0, a1, fmaxf(s[126], s[127]));
         } else {
-          float a0 = fminf(s[0], s[1]), a1 = fminf(s[2], s[3]);
-          float a2 = fminf(s[4], s[5]), a3 = fminf(s[6], s[7]);
+          float a0 = min3(s[0], s[1], s[2]), a1 = min3(s[3], s[4], s[5]);
 #pragma unroll
-          for (int c = 8; c < 128; c += 8) {
-            a0 = fminf(a0, fminf(s[c], s[c + 1]));
-            a1 = fminf(a1, fminf(s[c + 2], s[c + 3]));
-            a2 = fminf(a2, fminf(s[c + 4], s[c + 5]));
-            a3 = fminf(a3, fminf(s[c + 6], s[c + 7]));
+          for (int c = 6; c < 126; c += 4) {
+            a0 = min3(a0, s[c], s[c + 1]);
+            a1 = min3(a1, s[c + 2], s[c + 3]);
           }
-          red = fminf(fminf(a0, a1), fminf(a2, a3));
+          red = min3(a0, a1, fminf(s[126], s[127]));
         }
         const float m_cand = red * sl2;
         float alpha = 1.f;
@@ -526,18 +520,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           m = m_cand;
         }
         const float neg_m = (m == -INFINITY) ? 0.f : -m;
-        float sum0 = 0.f, sum1 = 0.f;
+        // x = s·sl2 − m and the row sums on packed fp32 pairs.
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(neg_m, neg_m);
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const float x = fmaf(s[c], sl2, neg_m);
-          s[c] = ex2(x);
+        for (int c = 0; c < 64; ++c) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(s[2 * c], s[2 * c + 1]), sl2x2, negm2), x0, x1);
+          s[2 * c] = ex2(x0);
+          s[2 * c + 1] = ex2(x1);
         }
+        uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
         if constexpr (!FP8) {
           uint32_t pk[64];
 #pragma unroll
           for (int c = 0; c < 64; ++c) {
-            sum0 += s[2 * c];
-            sum1 += s[2 * c + 1];
+            const uint64_t pr = f2_pack(s[2 * c], s[2 * c + 1]);
+            if (c & 1) acc1 = f2_add(acc1, pr); else acc0 = f2_add(acc0, pr);
             pk[c] = pack_bf16(s[2 * c], s[2 * c + 1]);
           }
           tmem_st32(tS + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
@@ -546,13 +544,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t pk[32];
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
-            sum0 += s[4 * c] + s[4 * c + 2];
-            sum1 += s[4 * c + 1] + s[4 * c + 3];
+            acc0 = f2_add(acc0, f2_pack(s[4 * c], s[4 * c + 1]));
+            acc1 = f2_add(acc1, f2_pack(s[4 * c + 2], s[4 * c + 3]));
             pk[c] = pack_e4m3x4(s[4 * c], s[4 * c + 1], s[4 * c + 2], s[4 * c + 3]);
           }
           tmem_st32(tS + 0, pk);
         }
-        l = l * alpha + (sum0 + sum1);
+        float q0, q1;
+        f2_unpack(f2_add(acc0, acc1), q0, q1);
+        l = l * alpha + (q0 + q1);
         const bool need = (j > 0) && (alpha != 1.f);
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
