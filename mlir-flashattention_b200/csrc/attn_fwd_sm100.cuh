@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_ready[t], 128);
+      mbar_init(&p_ready[t], 4);  // one arrival per softmax warp
       mbar_init(&pv_done[t], 1);
       mbar_init(&o_free[t], 128);
     }
@@ -307,6 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t dQ0 = make_sdesc(smem_u32(sQ), 16, 1024);
     const uint64_t dK0 = make_sdesc(smem_u32(sKV), 16, 1024);
     const uint64_t dV0 = make_sdesc(smem_u32(sKV), C::kBoxBytes, 1024);
+    const uint32_t lead = elect_one();  // the lane that issues MMAs and commits
     auto issue_S = [&](int t, int stage) {
       const uint64_t a0 = dQ0 + static_cast<uint64_t>((t * C::kTileBytes) >> 4);
       const uint64_t b0 = dK0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
@@ -314,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kk = 0; kk < C::kKStepsS; ++kk) {
         constexpr int kBox = C::kBoxBytes;
         const uint32_t off = ((kk * 32) / 128) * kBox + ((kk * 32) % 128);
-        mma_ss_warp<C::kKind>(tmem + t * 128, a0 + (off >> 4), b0 + (off >> 4), idS,
+        mma_ss_lead<C::kKind>(lead, tmem + t * 128, a0 + (off >> 4), b0 + (off >> 4), idS,
                               kk > 0 ? 1u : 0u);
       }
     };
@@ -322,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t b0 = dV0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
 #pragma unroll
       for (int kk = 0; kk < C::kKStepsPV; ++kk)
-        mma_ts_warp<C::kKind>(tmem + 256 + t * D, tmem + t * 128 + kk * 8,
+        mma_ts_lead<C::kKind>(lead, tmem + 256 + t * D, tmem + t * 128 + kk * 8,
                               b0 + static_cast<uint64_t>((kk * C::kKeysPerStep * 128) >> 4), idO,
                               (acc || kk > 0) ? 1u : 0u);
     };
@@ -360,11 +361,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         issue_S(t, kst(0));
-        mma_commit_warp(&s_full[t]);
+        mma_commit_lead(lead, &s_full[t]);
       }
       if (!ok) break;
-      mma_commit_warp(&kv_empty[kst(0)]);        // K_0 free once both S GEMMs finish
-      if (nmax == 1) mma_commit_warp(q_empty);  // every S GEMM of this pair is issued
+      mma_commit_lead(lead, &kv_empty[kst(0)]);        // K_0 free once both S GEMMs finish
+      if (nmax == 1) mma_commit_lead(lead, q_empty);  // every S GEMM of this pair is issued
       // Per KV step j, for each Q tile t in turn: O_t += P_t(j)·V_j, then
       // S_t(j+1) = Q_t·K_{j+1}ᵀ as soon as that P·V GEMM has finished reading
       // P_t(j) (P lives in the S_t columns).  Tile t's next softmax then
@@ -390,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           issue_PV(t, vst(j), j > 0);
-          mma_commit_warp(&pv_done[t]);
+          mma_commit_lead(lead, &pv_done[t]);
           ++pv_cnt[t];
           if (j + 1 < n_t[t]) {
             if (!k_next) {
@@ -406,18 +407,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             issue_S(t, kst(j + 1));
-            mma_commit_warp(&s_full[t]);
+            mma_commit_lead(lead, &s_full[t]);
           }
         }
         if (!ok) break;
-        mma_commit_warp(&kv_empty[vst(j)]);  // V_j free once the P·V GEMMs finish
+        mma_commit_lead(lead, &kv_empty[vst(j)]);  // V_j free once the P·V GEMMs finish
         if (j + 1 < nmax) {
           if (!k_next && !wait(&kv_full[kst(j + 1)], kph(j + 1))) {
             ok = false;
             break;
           }
-          mma_commit_warp(&kv_empty[kst(j + 1)]);  // K_{j+1} free once its S GEMMs finish
-          if (j + 2 == nmax) mma_commit_warp(q_empty);
+          mma_commit_lead(lead, &kv_empty[kst(j + 1)]);  // K_{j+1} free once its S GEMMs finish
+          if (j + 2 == nmax) mma_commit_lead(lead, q_empty);
         }
       }
       for (int t = 0; t < 2; ++t)
@@ -426,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++qi;
     }
     // Drain every MMA this warp issued before TMEM is released.
-    mma_commit_warp(drain);
+    mma_commit_lead(lead, drain);
     if (lane == 0) drain_wait(drain, 0, p.status);
     __syncwarp();
   } else {
@@ -567,7 +568,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_ready[t]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_ready[t]);
       }
       if (!ok) break;
       // -------------------------------------------------------- epilogue

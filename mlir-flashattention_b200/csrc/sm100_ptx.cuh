@@ -211,6 +211,69 @@ __device__ __forceinline__ void mma_ts_warp(uint32_t d_tmem, uint32_t a_tmem, ui
   }
 }
 
+// One elected lane for a batch of issues: returns 1 on exactly one lane of
+// the (converged) warp.
+__device__ __forceinline__ uint32_t elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(pred));
+  return pred;
+}
+
+// MMA forms predicated on a precomputed leader flag (see elect_one).
+template <int KIND>
+__device__ __forceinline__ void mma_ss_lead(uint32_t lead, uint32_t d_tmem, uint64_t a_desc,
+                                            uint64_t b_desc, uint32_t idesc, uint32_t acc) {
+  if constexpr (KIND == 0) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 e, %5, 0;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc), "r"(lead));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 e, %5, 0;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc), "r"(lead));
+  }
+}
+
+template <int KIND>
+__device__ __forceinline__ void mma_ts_lead(uint32_t lead, uint32_t d_tmem, uint32_t a_tmem,
+                                            uint64_t b_desc, uint32_t idesc, uint32_t acc) {
+  if constexpr (KIND == 0) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 e, %5, 0;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc), "r"(lead));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 e, %5, 0;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc), "r"(lead));
+  }
+}
+
+__device__ __forceinline__ void mma_commit_lead(uint32_t lead, uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %1, 0;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar)),
+      "r"(lead)
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_commit_warp(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
