@@ -239,6 +239,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--validate", action="store_true",
+                    help="after timing, gather each rank's first slice (Q, K, V, sampled O "
+                         "tiles) to rank 0 over the process group and check it against the oracle")
     ap.add_argument("--heads", type=int, default=None,
                     help="override the query-head count (reduced profiling case)")
     args = ap.parse_args()
@@ -337,12 +340,54 @@ def main():
         e2e = run_e2e(args, pkg, w, q, k, v, out, (qd, kd, vd), B, Hq, job_flops, world, dev,
                       odt, dist)
 
+    validation = None
+    if args.validate:
+        validation = validate_gathered(w, q, k, v, out, rank, world, qd, kd, vd)
+
     if rank == 0:
-        emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e)
+        emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validation)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def validate_gathered(w, q, k, v, out, rank, world, qd, kd, vd):
+    """Gather every rank's first (batch, head) slice — Q, its K/V head and the
+    output rows of sampled Q tiles — to rank 0 (all_gather on the process
+    group: NCCL over NVLink between GPUs) and compare with the oracle there.
+    Runs outside the timed region."""
+    import numpy as np  # noqa: PLC0415
+    import torch  # noqa: PLC0415
+    import __graft_entry__ as ge  # noqa: PLC0415
+    from mlir_flashattention_b200 import sharding  # noqa: PLC0415
+
+    tiles = list(range(3, (w.N + 127) // 128, 31))
+    rows = torch.cat([torch.arange(t * 128, min(w.N, t * 128 + 128)) for t in tiles]).to(q.device)
+
+    def as_f32(x, s):
+        return x.float() * s
+
+    payload = [as_f32(q[0, 0], qd), as_f32(k[0, 0], kd), as_f32(v[0, 0], vd),
+               out[0, 0].float().index_select(0, rows)]
+    if world > 1:
+        gathered = [sharding.gather_rows(t.contiguous(), world, rank) for t in payload]
+    else:
+        gathered = [[t] for t in payload]
+    if rank != 0:
+        return None
+    o = ge.oracle()
+    worst = 0.0
+    for r in range(world):
+        Q, K, V, Og = (g[r].cpu().numpy() for g in gathered)
+        ref = np.zeros((1, 1, w.N, w.D), np.float32)
+        o.attn_batched(Q[None, None], K[None, None], V[None, None], w.scale, causal=w.causal,
+                       tile_offset=tiles[0], tile_stride=31, out=ref, nthreads=host_threads())
+        R = ref[0, 0][rows.cpu().numpy()]
+        worst = max(worst, float(np.abs(Og - R).max() / np.abs(R).max()))
+    return {"max_rel_err": worst, "tol": w.tol, "passed": worst <= w.tol,
+            "checked": f"{world} rank(s) x slice 0 x {len(tiles)} Q tiles",
+            "gather": "all_gather over the process group (NCCL)" if world > 1 else "local"}
 
 
 def run_e2e(args, pkg, w, q, k, v, out, descales, B, Hq, job_flops, world, dev, odt, dist):
@@ -391,7 +436,7 @@ def run_e2e(args, pkg, w, q, k, v, out, descales, B, Hq, job_flops, world, dev, 
             "path": "_mlir_ciface_attn_fused_*_4d with pinned host memrefs"}
 
 
-def emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e):
+def emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validation=None):
     peaks, peak_src = load_peaks()
     kernel_ms = ms / args.steps  # one launch per step on this rank
     achieved = w.flops(slices) / (kernel_ms * 1e-3) / 1e12
@@ -419,6 +464,8 @@ def emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e):
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if validation is not None:
+        line["validation"] = validation
     if world == 1 and not args.no_cpu_baseline:
         tf, cores, text = cpu_sample(w)
         line["cpu_baseline"] = {"value": tf, "unit": "TFLOP/s", "cores": cores,

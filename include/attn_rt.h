@@ -13,7 +13,7 @@
  * Semantics of one (batch, head) slice, identical to the reference op:
  *   O = softmax(Q·Kᵀ·scale, masked entries -> -inf) · V
  * The reference op is rank-2 f32 only; this ABI adds rank-4 [B,H,N,D] views,
- * bf16 and fp8-e4m3 inputs (fp32 accumulation), grouped-query heads (Hq a
+ * bf16, f16 and fp8-e4m3 inputs (fp32 accumulation), grouped-query heads (Hq a
  * multiple of Hkv), and an optional log-sum-exp output.
  *
  * Ownership and threading.  The caller owns every buffer; O (and LSE) are
@@ -58,6 +58,7 @@ extern "C" {
 #define ATTN_F32   0
 #define ATTN_BF16  1
 #define ATTN_E4M3  2
+#define ATTN_F16   3
 
 #define ATTN_MASK_NONE    0  /* no mask operand                                   */
 #define ATTN_MASK_CAUSAL  1  /* mask[i][j] = (j > i): the causal generic           */
@@ -70,8 +71,8 @@ extern "C" {
  * All data pointers are device pointers.
  */
 typedef struct AttnDesc {
-  int32_t dtype;        /* ATTN_F32 / ATTN_BF16 / ATTN_E4M3: type of Q, K, V   */
-  int32_t out_dtype;    /* ATTN_F32 or ATTN_BF16: type of O                    */
+  int32_t dtype;        /* ATTN_F32 / ATTN_BF16 / ATTN_F16 / ATTN_E4M3: Q, K, V  */
+  int32_t out_dtype;    /* ATTN_F32, ATTN_BF16 or ATTN_F16: type of O           */
   int32_t mask_kind;    /* ATTN_MASK_*                                          */
   int32_t flags;        /* reserved, must be 0                                  */
   int64_t B, Hq, Hkv, Nq, Nk, D;
@@ -166,6 +167,12 @@ ATTN_API int32_t _mlir_ciface_attn_fused_bf16_nomask_4d(AttnMemRef4D* Q, AttnMem
                                                float scale, AttnMemRef4D* O, AttnMemRef4D* LSE);
 ATTN_API int32_t _mlir_ciface_attn_fused_bf16_causal_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
                                                float scale, AttnMemRef4D* O, AttnMemRef4D* LSE);
+
+/* Rank-4 f16 in / f16 out (same kernels, f16 operand format). */
+ATTN_API int32_t _mlir_ciface_attn_fused_f16_nomask_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
+                                                       float scale, AttnMemRef4D* O, AttnMemRef4D* LSE);
+ATTN_API int32_t _mlir_ciface_attn_fused_f16_causal_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
+                                                       float scale, AttnMemRef4D* O, AttnMemRef4D* LSE);
 
 /* Rank-4 bf16 with a general i1 mask memref<BxHxNqxNkxi1> (one byte per
  * element, 1 = masked; batch/head strides may be 0 to broadcast one mask);

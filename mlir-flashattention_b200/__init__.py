@@ -21,13 +21,13 @@ import os
 __all__ = [
     "AttentionError", "VerifyError", "fused", "classify_mask", "lib", "launch_count",
     "check_status", "AttnDesc", "AttnMemRef2D", "AttnMemRef4D", "memref", "shard_slices",
-    "ATTN_F32", "ATTN_BF16", "ATTN_E4M3", "MASK_NONE", "MASK_CAUSAL", "MASK_DENSE",
+    "ATTN_F32", "ATTN_BF16", "ATTN_E4M3", "ATTN_F16", "MASK_NONE", "MASK_CAUSAL", "MASK_DENSE",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libattnrt.so")
 
-ATTN_F32, ATTN_BF16, ATTN_E4M3 = 0, 1, 2
+ATTN_F32, ATTN_BF16, ATTN_E4M3, ATTN_F16 = 0, 1, 2, 3
 MASK_NONE, MASK_CAUSAL, MASK_DENSE = 0, 1, 2
 
 STATUS = {
@@ -112,6 +112,8 @@ def lib():
             fn.restype, fn.argtypes = ctypes.c_int32, [m4, m4, m4, f, m4]
             fn = getattr(L, f"_mlir_ciface_attn_fused_bf16_{name}_4d")
             fn.restype, fn.argtypes = ctypes.c_int32, [m4, m4, m4, f, m4, m4]
+            fn = getattr(L, f"_mlir_ciface_attn_fused_f16_{name}_4d")
+            fn.restype, fn.argtypes = ctypes.c_int32, [m4, m4, m4, f, m4, m4]
             fn = getattr(L, f"_mlir_ciface_attn_fused_e4m3_{name}_4d")
             fn.restype, fn.argtypes = ctypes.c_int32, [m4, m4, m4, f, f, f, f, m4, m4]
         L._mlir_ciface_attn_fused_bf16_mask_4d.restype = ctypes.c_int32
@@ -153,6 +155,8 @@ def _dtype_code(t):
         return ATTN_F32
     if t.dtype == torch.bfloat16:
         return ATTN_BF16
+    if t.dtype == torch.float16:
+        return ATTN_F16
     if t.dtype in (torch.float8_e4m3fn, torch.uint8):
         return ATTN_E4M3
     raise VerifyError(f"unsupported element type {t.dtype}")
@@ -214,7 +218,7 @@ def fused(Q, K, V, scale, mask=None, output=None, *, causal=False, lse=None,
     if _dtype_code(K) != dt or _dtype_code(V) != dt:
         raise VerifyError("Q, K and V must share one element type")
     if output is None:
-        odt = torch.float32 if dt == ATTN_F32 else torch.bfloat16
+        odt = {ATTN_F32: torch.float32, ATTN_F16: torch.float16}.get(dt, torch.bfloat16)
         output = torch.empty(Q.shape, dtype=odt, device=Q.device)
     o4 = _as4(output, "output", "seq_q", "head_dim")
     if o4.shape[2] != Nq:
@@ -242,7 +246,7 @@ def fused(Q, K, V, scale, mask=None, output=None, *, causal=False, lse=None,
             raise VerifyError(f"{n} must be a CUDA tensor")
     d = AttnDesc()
     d.dtype = dt
-    d.out_dtype = ATTN_F32 if output.dtype == torch.float32 else ATTN_BF16
+    d.out_dtype = {torch.float32: ATTN_F32, torch.float16: ATTN_F16}.get(output.dtype, ATTN_BF16)
     d.mask_kind = mask_kind
     d.B, d.Hq, d.Hkv, d.Nq, d.Nk, d.D = B, Hq, k4.shape[1], Nq, k4.shape[2], D
     for dst, t in ((d.q_stride, q4), (d.k_stride, k4), (d.v_stride, v4), (d.o_stride, o4)):

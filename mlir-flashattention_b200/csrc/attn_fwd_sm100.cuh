@@ -52,7 +52,7 @@ struct FwdParams {
   int num_bh;                // B * Hq
   float scale_log2;          // scale * log2(e) (* q/k descales for e4m3)
   float o_scale;             // v descale for e4m3, else 1
-  int out_f32;               // 1: O is fp32, 0: O is bf16
+  int out_kind;              // 0: O is bf16, 1: fp32, 2: f16
   // Dense i1 mask (one byte per element, 1 = masked), mode 2 only.
   const uint8_t* mask;
   int64_t m_sb, m_sh, m_sn;  // byte strides: batch, head, row (column stride 1)
@@ -64,8 +64,14 @@ constexpr int kMaskNone = 0;    // no mask operand
 constexpr int kMaskCausal = 1;  // mask[i][j] = j > i, computed
 constexpr int kMaskDense = 2;   // explicit i1 mask read from memory
 
-template <int D, bool FP8>
+// Input element types of the tensor-core kernel.
+constexpr int kEltBF16 = 0;
+constexpr int kEltE4M3 = 1;
+constexpr int kEltF16 = 2;
+
+template <int D, int ELT>
 struct FwdCfg {
+  static constexpr bool FP8 = ELT == kEltE4M3;
   static constexpr int kEB = FP8 ? 1 : 2;               // bytes per input element
   static constexpr int kBoxCols = 128 / kEB;            // elements per 128-byte row
   static constexpr int kNBox = (D * kEB) / 128;         // 128-byte column boxes per tile
@@ -75,7 +81,8 @@ struct FwdCfg {
   static constexpr int kKStepsS = (D * kEB) / 32;       // 32 bytes of K per MMA
   static constexpr int kKeysPerStep = 32 / kEB;         // keys per P·V MMA
   static constexpr int kKStepsPV = 128 / kKeysPerStep;
-  static constexpr uint32_t kFmt = FP8 ? 0u : 1u;       // e4m3 : bf16
+  // Operand format field: kind::f16 has F16 = 0, BF16 = 1; kind::f8f6f4 E4M3 = 0.
+  static constexpr uint32_t kFmt = ELT == kEltBF16 ? 1u : 0u;
   static constexpr int kKind = FP8 ? 1 : 0;
   static constexpr int kPCols = 128 * kEB / 4;          // TMEM columns holding P
   static constexpr int kNumBars = 2 + 2 * kStages + 2 + 2 + 2 + 2 + 1;
@@ -176,14 +183,15 @@ __device__ __forceinline__ void load_mask_row(const uint8_t* mrow, int kbase, in
   }
 }
 
-template <int D, int MODE, bool FP8>
+template <int D, int MODE, int ELT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   constexpr bool CAUSAL = MODE == kMaskCausal;
   constexpr bool DENSE = MODE == kMaskDense;
-  using C = FwdCfg<D, FP8>;
+  using C = FwdCfg<D, ELT>;
+  constexpr bool FP8 = C::FP8;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -537,7 +545,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < 64; ++c) {
             const uint64_t pr = f2_pack(s[2 * c], s[2 * c + 1]);
             if (c & 1) acc1 = f2_add(acc1, pr); else acc0 = f2_add(acc0, pr);
-            pk[c] = pack_bf16(s[2 * c], s[2 * c + 1]);
+            pk[c] = ELT == kEltF16 ? pack_f16(s[2 * c], s[2 * c + 1])
+                                   : pack_bf16(s[2 * c], s[2 * c + 1]);
           }
           tmem_st32(tS + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
           tmem_st32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
@@ -594,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&o_free[t]);
         }
         if (live) {
-          if (p.out_f32) {
+          if (p.out_kind == 1) {
             float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + obase + c * 32);
 #pragma unroll
             for (int i = 0; i < 8; ++i)
@@ -604,17 +613,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    __uint_as_float(o[4 * i + 3]) * inv_l);
           } else {
             uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.o) + obase + c * 32);
+            const bool f16 = p.out_kind == 2;
+            auto pk2 = [&](int e) {
+              const float a = __uint_as_float(o[e]) * inv_l, bb = __uint_as_float(o[e + 1]) * inv_l;
+              return f16 ? pack_f16(a, bb) : pack_bf16(a, bb);
+            };
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               uint4 v;
-              v.x = pack_bf16(__uint_as_float(o[8 * i + 0]) * inv_l,
-                              __uint_as_float(o[8 * i + 1]) * inv_l);
-              v.y = pack_bf16(__uint_as_float(o[8 * i + 2]) * inv_l,
-                              __uint_as_float(o[8 * i + 3]) * inv_l);
-              v.z = pack_bf16(__uint_as_float(o[8 * i + 4]) * inv_l,
-                              __uint_as_float(o[8 * i + 5]) * inv_l);
-              v.w = pack_bf16(__uint_as_float(o[8 * i + 6]) * inv_l,
-                              __uint_as_float(o[8 * i + 7]) * inv_l);
+              v.x = pk2(8 * i + 0);
+              v.y = pk2(8 * i + 2);
+              v.z = pk2(8 * i + 4);
+              v.w = pk2(8 * i + 6);
               dst[i] = v;
             }
           }

@@ -173,10 +173,11 @@ int sm_count(int* out) {
 }
 
 // -------------------------------------------------------------- launches
-template <int D, int MODE, bool FP8>
+template <int D, int MODE, int ELT>
 int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
-  using C = attn_sm100::FwdCfg<D, FP8>;
-  auto kern = attn_sm100::attn_fwd_sm100_kernel<D, MODE, FP8>;
+  using C = attn_sm100::FwdCfg<D, ELT>;
+  constexpr bool FP8 = C::FP8;
+  auto kern = attn_sm100::attn_fwd_sm100_kernel<D, MODE, ELT>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -185,7 +186,9 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute");
   const CUtensorMapDataType dt =
-      FP8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+      FP8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+          : (ELT == attn_sm100::kEltF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                        : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
   const int eb = FP8 ? 1 : 2;
   CUtensorMap mq, mk, mv;
   int rc;
@@ -215,7 +218,7 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
   if (sl2 == 0.f) sl2 = 1e-30f;  // scale 0: uniform weights without 0*inf
   p.scale_log2 = sl2;
   p.o_scale = FP8 ? d.v_descale : 1.f;
-  p.out_f32 = d.out_dtype == ATTN_F32 ? 1 : 0;
+  p.out_kind = d.out_dtype == ATTN_F32 ? 1 : (d.out_dtype == ATTN_F16 ? 2 : 0);
   if (MODE == attn_sm100::kMaskDense) {
     p.mask = d.mask;
     p.m_sb = d.mask_stride[0];
@@ -320,11 +323,12 @@ int validate(const AttnDesc& d) {
       if (d.D > 256) return fail(ATTN_ERR_UNSUPPORTED, "f32 path supports head_dim <= 256");
       return ATTN_OK;
     case ATTN_BF16:
+    case ATTN_F16:
     case ATTN_E4M3: {
-      if (d.out_dtype != ATTN_BF16 && d.out_dtype != ATTN_F32)
-        return fail(ATTN_ERR_DTYPE, "output must be bf16 or f32");
-      if (d.dtype == ATTN_BF16 && d.D != 64 && d.D != 128)
-        return fail(ATTN_ERR_UNSUPPORTED, "bf16 path supports head_dim 64 or 128 (got %lld)",
+      if (d.out_dtype != ATTN_BF16 && d.out_dtype != ATTN_F32 && d.out_dtype != ATTN_F16)
+        return fail(ATTN_ERR_DTYPE, "output must be bf16, f16 or f32");
+      if (d.dtype != ATTN_E4M3 && d.D != 64 && d.D != 128)
+        return fail(ATTN_ERR_UNSUPPORTED, "bf16/f16 path supports head_dim 64 or 128 (got %lld)",
                     (long long)d.D);
       if (d.dtype == ATTN_E4M3 && d.D != 128)
         return fail(ATTN_ERR_UNSUPPORTED, "e4m3 path supports head_dim 128 (got %lld)",
@@ -345,12 +349,12 @@ int validate(const AttnDesc& d) {
   }
 }
 
-template <int D, bool FP8>
+template <int D, int ELT>
 int dispatch_mode(const AttnDesc& d, int32_t* status, cudaStream_t s) {
   switch (d.mask_kind) {
-    case ATTN_MASK_CAUSAL: return launch_sm100<D, attn_sm100::kMaskCausal, FP8>(d, status, s);
-    case ATTN_MASK_DENSE: return launch_sm100<D, attn_sm100::kMaskDense, FP8>(d, status, s);
-    default: return launch_sm100<D, attn_sm100::kMaskNone, FP8>(d, status, s);
+    case ATTN_MASK_CAUSAL: return launch_sm100<D, attn_sm100::kMaskCausal, ELT>(d, status, s);
+    case ATTN_MASK_DENSE: return launch_sm100<D, attn_sm100::kMaskDense, ELT>(d, status, s);
+    default: return launch_sm100<D, attn_sm100::kMaskNone, ELT>(d, status, s);
   }
 }
 
@@ -360,9 +364,14 @@ int dispatch(const AttnDesc& d, int32_t* status, cudaStream_t s) {
     if (d.D <= 128) return launch_f32<128>(d, s);
     return launch_f32<256>(d, s);
   }
+  using namespace attn_sm100;
   if (d.dtype == ATTN_BF16)
-    return d.D == 64 ? dispatch_mode<64, false>(d, status, s) : dispatch_mode<128, false>(d, status, s);
-  return dispatch_mode<128, true>(d, status, s);
+    return d.D == 64 ? dispatch_mode<64, kEltBF16>(d, status, s)
+                     : dispatch_mode<128, kEltBF16>(d, status, s);
+  if (d.dtype == ATTN_F16)
+    return d.D == 64 ? dispatch_mode<64, kEltF16>(d, status, s)
+                     : dispatch_mode<128, kEltF16>(d, status, s);
+  return dispatch_mode<128, kEltE4M3>(d, status, s);
 }
 
 // ------------------------------------------------- memref-descriptor layer
@@ -447,7 +456,9 @@ AttnDesc desc_from_views(int dtype, int out_dtype, int mask_kind, const View& Q,
   return d;
 }
 
-size_t elem_bytes(int dt) { return dt == ATTN_F32 ? 4 : dt == ATTN_BF16 ? 2 : 1; }
+size_t elem_bytes(int dt) {
+  return dt == ATTN_F32 ? 4 : (dt == ATTN_BF16 || dt == ATTN_F16) ? 2 : 1;
+}
 
 int ensure(void** p, size_t* have, size_t need) {
   if (*have >= need) return ATTN_OK;
@@ -765,6 +776,18 @@ F32_4D(_mlir_ciface_attn_fused_f32_causal_4d, ATTN_MASK_CAUSAL)
   }
 BF16_4D(_mlir_ciface_attn_fused_bf16_nomask_4d, ATTN_MASK_NONE)
 BF16_4D(_mlir_ciface_attn_fused_bf16_causal_4d, ATTN_MASK_CAUSAL)
+
+#define F16_4D(NAME, KIND)                                                                   \
+  int32_t NAME(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V, float scale,               \
+               AttnMemRef4D* O, AttnMemRef4D* LSE) {                                         \
+    if (!Q || !K || !V || !O) return fail(ATTN_ERR_INVALID, "null memref descriptor");        \
+    View L;                                                                                  \
+    if (LSE) L = view4(LSE, 4);                                                              \
+    return run_views(ATTN_F16, ATTN_F16, KIND, view4(Q, 2), view4(K, 2), view4(V, 2),         \
+                     view4(O, 2), scale, 1.f, 1.f, 1.f, LSE ? &L : nullptr, nullptr);         \
+  }
+F16_4D(_mlir_ciface_attn_fused_f16_nomask_4d, ATTN_MASK_NONE)
+F16_4D(_mlir_ciface_attn_fused_f16_causal_4d, ATTN_MASK_CAUSAL)
 
 int32_t _mlir_ciface_attn_fused_bf16_mask_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
                                              float scale, AttnMemRef4D* mask, AttnMemRef4D* O,

@@ -419,6 +419,13 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return r;
 }
 
+// Pack two floats into f16x2 with round-to-nearest-even; `lo` in bits 0..15.
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 // Pack four floats into e4m3x4 (satfinite, RNE); element 0 in bits 0..7.
 __device__ __forceinline__ uint32_t pack_e4m3x4(float a0, float a1, float a2, float a3) {
   uint16_t lo, hi;

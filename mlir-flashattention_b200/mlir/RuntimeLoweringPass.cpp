@@ -118,6 +118,7 @@ static MaskKind classifyMask(Value mask) {
 static StringRef dtypeName(Type t) {
   if (t.isF32()) return "f32";
   if (t.isBF16()) return "bf16";
+  if (t.isF16()) return "f16";
   if (isa<Float8E4M3FNType>(t)) return "e4m3";
   return "";
 }
@@ -137,7 +138,7 @@ struct FusedToRuntimeCall : public OpRewritePattern<FusedOp> {
       return op.emitOpError("a general i1 mask is supported for rank-2 f32 and rank-4 bf16 "
                             "operands");
     if (dt != "f32" && rank != 4)
-      return op.emitOpError("bf16/e4m3 operands are lowered in their rank-4 form");
+      return op.emitOpError("bf16/f16/e4m3 operands are lowered in their rank-4 form");
 
     std::string callee = ("attn_fused_" + dt + "_").str();
     callee += kind == MaskKind::None ? "nomask" : kind == MaskKind::Causal ? "causal" : "mask";

@@ -248,3 +248,42 @@ def test_bounded_wait_times_out_and_device_stays_usable(pkg, wl, oracle):
     got, _ = _run_pkg(pkg, wl, w, inp, True)
     ref, _ = _ref(oracle, inp, w, True)
     assert _rel(got, ref) <= 2e-2
+
+
+@pytest.mark.parametrize("Nq,Nk,causal", [(300, 700, False), (300, 700, True), (700, 300, True),
+                                          (128, 1024, False), (1000, 129, False)])
+def test_unequal_query_and_key_lengths(pkg, wl, oracle, Nq, Nk, causal):
+    """Cross-attention shapes (Nq != Nk), ragged tiles on both sides; causal
+    is the op's mask[i][j] = j > i (top-left aligned)."""
+    rng = np.random.Generator(np.random.PCG64(Nq * 7 + Nk))
+    B, H, D = 2, 2, 128
+    qf = wl.round_bf16(rng.standard_normal((B, H, Nq, D), dtype=np.float32))
+    kf = wl.round_bf16(rng.standard_normal((B, H, Nk, D), dtype=np.float32))
+    vf = wl.round_bf16(rng.standard_normal((B, H, Nk, D), dtype=np.float32))
+    q, k, v = (torch.from_numpy(a).cuda().to(torch.bfloat16) for a in (qf, kf, vf))
+    L = torch.empty((B, H, Nq), dtype=torch.float32, device="cuda")
+    out = pkg.fused(q, k, v, D ** -0.5, causal=causal, lse=L)
+    pkg.check_status(0)
+    ref, ref_lse = oracle.attn_batched(qf, kf, vf, D ** -0.5, causal=causal)
+    assert _rel(out.float().cpu().numpy(), ref) <= 2e-2
+    assert np.abs(L.cpu().numpy() - ref_lse).max() <= 1e-3
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [True, False])
+def test_f16_parity(pkg, oracle, D, causal):
+    """f16 inputs on the same tensor-core kernels (f16 operand format, P in
+    f16, f16 output), against the oracle on the f16-rounded values."""
+    rng = np.random.Generator(np.random.PCG64(D + 17 * causal))
+    B, H, N = 2, 2, 700
+    arrs = [rng.standard_normal((B, H, N, D), dtype=np.float32).astype(np.float16)
+            for _ in range(3)]
+    q, k, v = (torch.from_numpy(a).cuda() for a in arrs)
+    L = torch.empty((B, H, N), dtype=torch.float32, device="cuda")
+    out = pkg.fused(q, k, v, D ** -0.5, causal=causal, lse=L)
+    pkg.check_status(0)
+    assert out.dtype == torch.float16
+    ref, ref_lse = oracle.attn_batched(*(a.astype(np.float32) for a in arrs), D ** -0.5,
+                                       causal=causal)
+    assert _rel(out.float().cpu().numpy(), ref) <= 1e-2
+    assert np.abs(L.cpu().numpy() - ref_lse).max() <= 1e-3
