@@ -270,6 +270,10 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime  # noqa: PLC0415
+        # Keep rank 0's stdout to the one JSON line (NCCL's version banner
+        # goes to stdout when NCCL_DEBUG=VERSION).
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
