@@ -7,15 +7,20 @@
 // (lib/Attention/TilingPass.cpp:279-374: running max m, running sum l, O
 // rescaled by alpha = exp(m_old - m_new)), restated for the tensor cores:
 //
-//   CTA = two Q tiles of 128 rows (256 query rows) of one slice.
-//   warp 8      TMA producer: Q tiles once, then K_j / V_j tiles (128 keys)
-//               through an NS-stage shared-memory ring (mbarrier full/empty).
-//   warp 9      MMA issuer (one thread): S_t = Q_t·K_jᵀ into TMEM (SS form),
-//               O_t += P_t·V_j with P_t read from TMEM (TS form).
+//   Persistent: one CTA per SM walks a work list of Q-tile pairs (two Q
+//   tiles of 128 rows of one slice); see item_index / decode_item.
+//   warp 8      TMA producer: the pair's Q tiles, then K_j / V_j tiles (128
+//               keys) through an NS-stage shared-memory ring (mbarrier
+//               full/empty) that runs on across pairs.
+//   warp 9      MMA issuer (converged warp, one elected lane issues):
+//               S_t = Q_t·K_jᵀ into TMEM (SS form), O_t += P_t·V_j with P_t
+//               read from TMEM (TS form); order per KV step
+//               P·V_0(j), S_0(j+1), P·V_1(j), S_1(j+1).
 //   warps 0-3   softmax for Q tile 0, warps 4-7 for Q tile 1: one thread per
 //               query row reads its S row from TMEM, applies the mask, updates
-//               (m, l) in registers, writes P (bf16 / e4m3) back into the S
-//               columns and rescales its O row in TMEM when m moved.
+//               (m, l) in registers, writes P (bf16 / f16 / e4m3) back into the
+//               S columns and rescales its O row in TMEM when m moved; at the
+//               end of a pair it writes O / l and the LSE.
 //   The two Q tiles ping-pong: while one softmax group works, the tensor
 //   cores run the other tile's GEMMs.
 //
@@ -25,10 +30,11 @@
 // more than 2^8 (values of p stay <= 256, exact in bf16/e4m3 range), which
 // skips most O rescales; the final O/l and LSE are unaffected by the choice.
 //
-// Causal (the mask mask[i][j] = j > i): KV tiles wholly above the diagonal
-// are never loaded or multiplied (the FULL / MASKED / BOUNDARY tile split of
-// the reference design, Design.md:412-419); only diagonal and ragged-edge
-// tiles apply a per-element mask.
+// Mask modes: none; causal (mask[i][j] = j > i): KV tiles wholly above the
+// diagonal are never loaded or multiplied (the FULL / MASKED / BOUNDARY tile
+// split of the reference design, Design.md:412-419) and only diagonal and
+// ragged-edge tiles apply a per-element mask; dense: the op's i1 mask operand
+// (TilingPass.cpp:254-277) read per row and KV tile.
 //
 // Hang safety: every mbarrier wait is bounded (wall-clock limit); on expiry
 // the CTA records ATTN_ERR_TIMEOUT in the status word, all roles leave their
