@@ -487,7 +487,8 @@ int run_staged(const AttnDesc& hd, int device) {
   const size_t eb = elem_bytes(hd.dtype), ob = elem_bytes(hd.out_dtype);
   const int64_t group = hd.Hq / hd.Hkv;
   const int64_t ngroups = hd.B * hd.Hkv;
-  const int64_t per_chunk = std::max<int64_t>(1, (ngroups + 7) / 8);
+  // 16 chunks: measured best for c4 over PCIe (8: 9.65 ms, 16: 9.33, 32: 10.08).
+  const int64_t per_chunk = std::max<int64_t>(1, (ngroups + 15) / 16);
   const int64_t nchunks = (ngroups + per_chunk - 1) / per_chunk;
   const size_t q_slice = static_cast<size_t>(hd.Nq * hd.D) * eb;
   const size_t kv_slice = static_cast<size_t>(hd.Nk * hd.D) * eb;
