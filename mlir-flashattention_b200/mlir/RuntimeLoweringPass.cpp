@@ -28,6 +28,12 @@
 //   * anything else                                      -> "mask" (dense i1
 //     operand; rank-2 f32 or rank-4 bf16, others rejected with an error)
 //
+// Shapes: every memref operand is passed through `memref.cast` to the fully
+// dynamic strided type of its rank (memref<?x?xT, strided<[?, ?], offset: ?>>),
+// so one declaration per callee serves every static or dynamic shape and
+// layout in the module; the runtime reads sizes and strides from the
+// descriptor.  (TilingPass.cpp:168-172 accepts static shapes only.)
+//
 // The pass is stateless.  Unlike the reference's FuncOp-anchored passes
 // (AttentionPasses.td:14,27) it is anchored on the module, because it adds
 // the private runtime declarations at module scope, which a pass running
@@ -44,6 +50,7 @@
 #include "mlir/Dialect/Linalg/IR/Linalg.h"
 #include "mlir/Dialect/MemRef/IR/MemRef.h"
 #include "mlir/IR/BuiltinOps.h"
+#include "mlir/IR/BuiltinTypes.h"
 #include "mlir/IR/PatternMatch.h"
 #include "mlir/IR/SymbolTable.h"
 #include "mlir/Transforms/GreedyPatternRewriteDriver.h"
@@ -123,6 +130,14 @@ static StringRef dtypeName(Type t) {
   return "";
 }
 
+// The fully dynamic strided memref type of `t`'s rank and element type.
+static MemRefType dynamicStridedType(MemRefType t) {
+  const int64_t r = t.getRank();
+  SmallVector<int64_t> shape(r, ShapedType::kDynamic), strides(r, ShapedType::kDynamic);
+  auto layout = StridedLayoutAttr::get(t.getContext(), ShapedType::kDynamic, strides);
+  return MemRefType::get(shape, t.getElementType(), layout, t.getMemorySpace());
+}
+
 struct FusedToRuntimeCall : public OpRewritePattern<FusedOp> {
   using OpRewritePattern::OpRewritePattern;
 
@@ -150,12 +165,22 @@ struct FusedToRuntimeCall : public OpRewritePattern<FusedOp> {
     // Signature first (no IR is created before every check has passed).
     auto f32 = rewriter.getF32Type();
     auto lseT = MemRefType::get({0, 0, 0, 1}, f32);  // zero-sized: LSE not requested
-    SmallVector<Type> argTypes = {op.getQ().getType(), op.getK().getType(),
-                                  op.getV().getType(), f32};
+    SmallVector<Value> memrefs = {op.getQ(), op.getK(), op.getV()};
+    if (kind == MaskKind::Dense) memrefs.push_back(op.getMask());
+    memrefs.push_back(op.getOutput());
+    SmallVector<Type> dynTypes;
+    for (Value v : memrefs) {
+      auto t = cast<MemRefType>(v.getType());
+      auto d = dynamicStridedType(t);
+      if (!memref::CastOp::areCastCompatible(t, d))
+        return op.emitOpError("operand layout is not strided: ") << t;
+      dynTypes.push_back(d);
+    }
+    auto lseDyn = dynamicStridedType(lseT);
+    SmallVector<Type> argTypes = {dynTypes[0], dynTypes[1], dynTypes[2], f32};
     if (dt == "e4m3") argTypes.append({f32, f32, f32});
-    if (kind == MaskKind::Dense) argTypes.push_back(op.getMask().getType());
-    argTypes.push_back(op.getOutput().getType());
-    if (dt != "f32") argTypes.push_back(lseT);
+    argTypes.append(dynTypes.begin() + 3, dynTypes.end());
+    if (dt != "f32") argTypes.push_back(lseDyn);
     auto fnType = rewriter.getFunctionType(argTypes, {rewriter.getI32Type()});
     auto fn = module.lookupSymbol<func::FuncOp>(callee);
     if (fn && fn.getFunctionType() != fnType)
@@ -169,7 +194,12 @@ struct FusedToRuntimeCall : public OpRewritePattern<FusedOp> {
     }
 
     rewriter.setInsertionPoint(op);
-    SmallVector<Value> args = {op.getQ(), op.getK(), op.getV(), op.getScale()};
+    auto toDyn = [&](Value v, Type d) -> Value {
+      if (v.getType() == d) return v;
+      return rewriter.create<memref::CastOp>(op.getLoc(), d, v);
+    };
+    SmallVector<Value> args = {toDyn(op.getQ(), dynTypes[0]), toDyn(op.getK(), dynTypes[1]),
+                               toDyn(op.getV(), dynTypes[2]), op.getScale()};
     if (dt == "e4m3") {
       // Per-tensor dequantisation factors ride on the op as optional f32
       // attributes (its attr-dict, AttentionOps.td:50); absent means 1.0.
@@ -180,9 +210,9 @@ struct FusedToRuntimeCall : public OpRewritePattern<FusedOp> {
             op.getLoc(), rewriter.getF32FloatAttr(static_cast<float>(val))));
       }
     }
-    if (kind == MaskKind::Dense) args.push_back(op.getMask());
-    args.push_back(op.getOutput());
-    if (dt != "f32") args.push_back(rewriter.create<memref::AllocaOp>(op.getLoc(), lseT));
+    for (size_t i = 3; i < memrefs.size(); ++i) args.push_back(toDyn(memrefs[i], dynTypes[i]));
+    if (dt != "f32")
+      args.push_back(toDyn(rewriter.create<memref::AllocaOp>(op.getLoc(), lseT), lseDyn));
     rewriter.create<func::CallOp>(op.getLoc(), fn, args);
     rewriter.eraseOp(op);
     return success();
