@@ -90,6 +90,19 @@ typedef struct AttnDesc {
   float v_descale;
   int32_t* status;           /* optional device word for kernel status; if null
                                 the runtime's per-device word is used            */
+  /* e4m3 only, optional (NULL = not used): per-block dequantisation factors,
+   * fp32 device arrays, contiguous, positive and finite, applied on top of the
+   * per-tensor factors above.  One block = 128 rows, the tile of the
+   * reference's TilingPass (AttentionPasses.td:46):
+   *   q_descale_blocks [B, Hq,  ceil(Nq / 128)]  Q rows [128 i, 128 i + 128)
+   *   k_descale_blocks [B, Hkv, ceil(Nk / 128)]  K rows [128 j, 128 j + 128)
+   *   v_descale_heads  [B, Hkv]                  all of V for one kv head
+   * Score (r, c) = scale * qd * kd * q_descale_blocks[b,h,r/128] *
+   * k_descale_blocks[b,h/(Hq/Hkv),c/128] * (Q8[r] . K8[c]); O is multiplied
+   * by vd * v_descale_heads[b,h/(Hq/Hkv)].  Device path (attn_fwd) only. */
+  const float* q_descale_blocks;
+  const float* k_descale_blocks;
+  const float* v_descale_heads;
 } AttnDesc;
 
 /* Asynchronous launch on `stream` (a cudaStream_t; NULL = legacy default).

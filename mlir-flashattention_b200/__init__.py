@@ -63,6 +63,8 @@ class AttnDesc(ctypes.Structure):
         ("scale", ctypes.c_float), ("q_descale", ctypes.c_float),
         ("k_descale", ctypes.c_float), ("v_descale", ctypes.c_float),
         ("status", ctypes.c_void_p),
+        ("q_descale_blocks", ctypes.c_void_p), ("k_descale_blocks", ctypes.c_void_p),
+        ("v_descale_heads", ctypes.c_void_p),
     ]
 
 
@@ -200,6 +202,10 @@ def fused(Q, K, V, scale, mask=None, output=None, *, causal=False, lse=None,
     place and returned (allocated if None: f32 for f32 inputs, else bf16).
     ``lse`` (optional, f32 [B, Hq, Nq] or [Nq]) receives the natural-log
     log-sum-exp of each row.  The launch is asynchronous on ``stream``.
+
+    e4m3 dequantisation factors are per tensor (Python floats) or per block
+    (f32 CUDA tensors): ``q_descale`` [B, Hq, ceil(Nq/128)] (one per 128-row
+    block of Q), ``k_descale`` [B, Hkv, ceil(Nk/128)], ``v_descale`` [B, Hkv].
     """
     import torch  # noqa: PLC0415
     q4 = _as4(Q, "Q", "seq_q", "head_dim")
@@ -260,7 +266,26 @@ def fused(Q, K, V, scale, mask=None, output=None, *, causal=False, lse=None,
         d.mask = m4.data_ptr()
         d.mask_stride[0], d.mask_stride[1], d.mask_stride[2] = m4.stride(0), m4.stride(1), m4.stride(2)
     d.scale = float(scale)
-    d.q_descale, d.k_descale, d.v_descale = float(q_descale), float(k_descale), float(v_descale)
+    Hkv, Nk = k4.shape[1], k4.shape[2]
+    shapes = {"q_descale": (B, Hq, -(-Nq // 128)), "k_descale": (B, Hkv, -(-Nk // 128)),
+              "v_descale": (B, Hkv)}
+    for name, val, field in (("q_descale", q_descale, "q_descale_blocks"),
+                             ("k_descale", k_descale, "k_descale_blocks"),
+                             ("v_descale", v_descale, "v_descale_heads")):
+        if isinstance(val, torch.Tensor):
+            if dt != ATTN_E4M3:
+                raise VerifyError(f"per-block {name} applies to float8_e4m3fn inputs")
+            want = shapes[name]
+            if Q.dim() == 2:
+                want = want[2:] if name != "v_descale" else ()
+            if (val.dtype != torch.float32 or not val.is_cuda or not val.is_contiguous()
+                    or tuple(val.shape) != tuple(want)):
+                raise VerifyError(f"per-block {name} must be a contiguous f32 CUDA tensor of "
+                                  f"shape {list(want)}")
+            setattr(d, field, val.data_ptr())
+            setattr(d, name, 1.0)
+        else:
+            setattr(d, name, float(val))
     with torch.cuda.device(Q.device):
         _raise(lib().attn_fwd(ctypes.byref(d), _stream_ptr(stream)))
         if sync_check:

@@ -63,6 +63,13 @@ struct FwdParams {
   const uint8_t* mask;
   int64_t m_sb, m_sh, m_sn;  // byte strides: batch, head, row (column stride 1)
   int mask_vec;              // 1: rows 16-byte aligned (vector loads)
+  // e4m3 per-block dequantisation factors (nullptr = not used): one per
+  // 128-row block of Q ([num_bh][nqb]) and of K ([B*Hkv][nkb]), one per
+  // kv head for V ([B*Hkv]).
+  const float* qd_blk;
+  const float* kd_blk;
+  const float* vd_head;
+  int nqb, nkb;
 };
 
 // Mask modes of the kernel (compile-time specialisations).
@@ -452,8 +459,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_off + t * 128;
     const uint32_t tO = tmem + lane_off + 256 + t * D;
-    const float sl2 = p.scale_log2;
-    const bool pos = sl2 >= 0.f;
+    const float sl2_base = p.scale_log2;  // scale·log2(e) (· per-tensor descales)
+    const bool pos = sl2_base >= 0.f;      // descales are positive: the sign is scale's
     const float mask_val = pos ? -INFINITY : INFINITY;
     int steps = 0;  // S tiles consumed so far (s_full / pv_done phases)
     bool ok = true;
@@ -470,6 +477,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = qs + r;
       float m = -INFINITY;
       float l = 0.f;
+      // e4m3 per-block factors: the Q block's folds into this tile's exponent
+      // scale, the K block's into each step's, the V head's into the epilogue.
+      float sl2_q = sl2_base, vd = 1.f, kd_cur = 1.f;
+      const float* kd_row = nullptr;
+      if constexpr (FP8) {
+        const int bk = b * (p.Hq / p.group) + h / p.group;
+        if (p.qd_blk) sl2_q *= __ldg(p.qd_blk + static_cast<int64_t>(itm.bh) * p.nqb + itm.pair * 2 + t);
+        if (p.vd_head) vd = __ldg(p.vd_head + bk);
+        if (p.kd_blk) {
+          kd_row = p.kd_blk + static_cast<int64_t>(bk) * p.nkb;
+          kd_cur = __ldg(kd_row);
+        }
+      }
       const uint8_t* mrow = nullptr;
       if constexpr (DENSE)
         mrow = p.mask + b * p.m_sb + h * p.m_sh + static_cast<int64_t>(min(row, p.Nq - 1)) * p.m_sn;
@@ -481,6 +501,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
+        float sl2 = sl2_q;
+        if constexpr (FP8) {
+          if (kd_row) {
+            sl2 *= kd_cur;
+            if (j + 1 < n) kd_cur = __ldg(kd_row + j + 1);  // next step's, loaded early
+          }
+        }
         float s[128];
         {
           uint32_t r0[32], r1[32], r2[32], r3[32];
@@ -594,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const float inv_l = p.o_scale / l;
+      const float inv_l = p.o_scale * vd / l;
       const int64_t obase = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
                             static_cast<int64_t>(row) * p.o_sn;
       const bool live = row < p.Nq;

@@ -218,6 +218,13 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
   if (sl2 == 0.f) sl2 = 1e-30f;  // scale 0: uniform weights without 0*inf
   p.scale_log2 = sl2;
   p.o_scale = FP8 ? d.v_descale : 1.f;
+  if (FP8) {
+    p.qd_blk = d.q_descale_blocks;
+    p.kd_blk = d.k_descale_blocks;
+    p.vd_head = d.v_descale_heads;
+    p.nqb = static_cast<int>((d.Nq + 127) / 128);
+    p.nkb = static_cast<int>((d.Nk + 127) / 128);
+  }
   p.out_kind = d.out_dtype == ATTN_F32 ? 1 : (d.out_dtype == ATTN_F16 ? 2 : 0);
   if (MODE == attn_sm100::kMaskDense) {
     p.mask = d.mask;
@@ -316,6 +323,12 @@ int validate(const AttnDesc& d) {
   if (d.mask_kind == ATTN_MASK_DENSE && !d.mask)
     return fail(ATTN_ERR_INVALID, "dense mask requested without a mask pointer");
   if (!std::isfinite(d.scale)) return fail(ATTN_ERR_INVALID, "scale must be finite");
+  const bool blocks = d.q_descale_blocks || d.k_descale_blocks || d.v_descale_heads;
+  if (blocks && d.dtype != ATTN_E4M3)
+    return fail(ATTN_ERR_DTYPE, "per-block descales apply to e4m3 inputs only");
+  for (const float* b : {d.q_descale_blocks, d.k_descale_blocks, d.v_descale_heads})
+    if ((reinterpret_cast<uintptr_t>(b) & 3u) != 0)
+      return fail(ATTN_ERR_ALIGN, "per-block descale arrays must be 4-byte aligned");
   switch (d.dtype) {
     case ATTN_F32:
       if (d.out_dtype != ATTN_F32)
@@ -676,7 +689,7 @@ int run_views(int dtype, int out_dtype, int mask_kind, const View& Q, const View
 // =================================================================== C ABI
 extern "C" {
 
-int attn_rt_version(void) { return (1 << 16) | 0; }
+int attn_rt_version(void) { return (1 << 16) | 1; }
 
 int64_t attn_rt_launch_count(void) { return g_launches.load(); }
 
@@ -866,6 +879,8 @@ extern "C" int attn_fwd_host_noalloc(const AttnDesc* desc, void* stream_) {
   const AttnDesc& hd = *desc;
   if (hd.mask_kind == ATTN_MASK_DENSE)
     return fail(ATTN_ERR_UNSUPPORTED, "attn_fwd_host_noalloc supports no-mask and causal calls");
+  if (hd.q_descale_blocks || hd.k_descale_blocks || hd.v_descale_heads)
+    return fail(ATTN_ERR_UNSUPPORTED, "attn_fwd_host_noalloc takes per-tensor descales only");
   int rc = validate(hd);
   if (rc != ATTN_OK) return rc;
   int dev = 0;

@@ -91,6 +91,38 @@ def quant_e4m3(x: np.ndarray):
     return y.view(np.uint8), float(descale), (y.astype(np.float32) * descale).astype(np.float32)
 
 
+def quant_e4m3_blocks(x: np.ndarray, block: int = 128):
+    """Per-block e4m3 quantisation of [B, H, N, D] along N (blocks of ``block``
+    rows, each scaled by its own amax/448).
+
+    Returns (codes uint8 [B,H,N,D], descales float32 [B,H,ceil(N/block)],
+    dequantised float32 [B,H,N,D]).
+    """
+    import ml_dtypes  # noqa: PLC0415
+
+    x = np.asarray(x, np.float32)
+    B, H, N, D = x.shape
+    nb = -(-N // block)
+    pad = np.zeros((B, H, nb * block, D), np.float32)
+    pad[:, :, :N] = x
+    blocks = pad.reshape(B, H, nb, block, D)
+    amax = np.abs(blocks).max(axis=(3, 4))
+    descale = np.where(amax > 0, amax / 448.0, 1.0).astype(np.float32)
+    y = np.clip(blocks / descale[..., None, None], -448.0, 448.0).astype(ml_dtypes.float8_e4m3fn)
+    deq = (y.astype(np.float32) * descale[..., None, None]).reshape(B, H, nb * block, D)[:, :, :N]
+    codes = y.view(np.uint8).reshape(B, H, nb * block, D)[:, :, :N]
+    return np.ascontiguousarray(codes), descale, np.ascontiguousarray(deq)
+
+
+def quant_e4m3_heads(x: np.ndarray):
+    """Per-(batch, head) e4m3 quantisation of [B, H, N, D].
+
+    Returns (codes uint8, descales float32 [B,H], dequantised float32).
+    """
+    codes, descale, deq = quant_e4m3_blocks(x, block=x.shape[2])
+    return codes, np.ascontiguousarray(descale[:, :, 0]), deq
+
+
 @dataclass
 class Inputs:
     """Host arrays for one workload.

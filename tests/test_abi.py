@@ -65,12 +65,20 @@ def _desc(pkg, **kw):
     ("mask_kind", 2, -1),    # dense without a mask pointer
     ("q", 0x10008, -5),      # misaligned
     ("flags", 1, -1),
+    ("k_descale_blocks", 0x20000, -4),  # per-block descales need e4m3 inputs
 ])
 def test_validation_codes(pkg, field, value, code):
     L = pkg.lib()
     d = _desc(pkg, **{field: value})
     assert L.attn_fwd(ctypes.byref(d), None) == code
     assert pkg.last_error()
+
+
+def test_block_descale_alignment(pkg):
+    """e4m3 with a misaligned per-block descale array is rejected before launch."""
+    d = _desc(pkg, dtype=pkg.ATTN_E4M3, q_descale_blocks=0x20002)
+    assert pkg.lib().attn_fwd(ctypes.byref(d), None) == -5
+    assert "4-byte" in pkg.last_error()
 
 
 def test_null_descriptor(pkg):

@@ -103,6 +103,45 @@ def test_e4m3_gqa_parity(pkg, wl, oracle):
     assert np.abs(lse - ref_lse).max() <= 1e-2
 
 
+@pytest.mark.parametrize("causal,nq,nk", [(True, 512, 512), (False, 300, 520), (True, 640, 384)])
+def test_e4m3_block_descales(pkg, wl, oracle, causal, nq, nk):
+    """e4m3 GQA with per-block Q/K and per-head V dequantisation factors.
+
+    Block magnitudes spread over two decades, so a factor applied to the wrong
+    block or head shows up as a large error; checked per (batch, head) slice.
+    """
+    rng = np.random.default_rng(11)
+    B, Hq, Hkv, D = 2, 8, 2, 128
+
+    def spread(n, H):
+        f = 10.0 ** rng.uniform(-1.0, 1.0, size=(B, H, -(-n // 128)))
+        return np.repeat(f, 128, axis=2)[:, :, :n, None].astype(np.float32)
+
+    q = rng.standard_normal((B, Hq, nq, D)).astype(np.float32) * spread(nq, Hq)
+    k = rng.standard_normal((B, Hkv, nk, D)).astype(np.float32) * spread(nk, Hkv)
+    v = rng.standard_normal((B, Hkv, nk, D)).astype(np.float32) * (
+        10.0 ** rng.uniform(-1.0, 1.0, size=(B, Hkv, 1, 1))).astype(np.float32)
+    q8, qd, qf = wl.quant_e4m3_blocks(q)
+    k8, kd, kf = wl.quant_e4m3_blocks(k)
+    v8, vd, vf = wl.quant_e4m3_heads(v)
+    scale = 1.0 / np.sqrt(D)
+    dev = [torch.from_numpy(a).cuda() for a in (q8, k8, v8, qd, kd, vd)]
+    L = torch.empty((B, Hq, nq), dtype=torch.float32, device="cuda")
+    out = pkg.fused(dev[0], dev[1], dev[2], scale, causal=causal, lse=L,
+                    q_descale=dev[3], k_descale=dev[4], v_descale=dev[5])
+    pkg.check_status(0)
+    got = out.float().cpu().numpy()
+    ref, ref_lse = oracle.attn_batched(qf, kf, vf, scale, causal=causal)
+    for b in range(B):
+        for h in range(Hq):
+            assert _rel(got[b, h], ref[b, h]) <= 6e-2, (b, h)
+    lse = L.cpu().numpy()
+    assert (np.abs(lse - ref_lse) <= 1e-2 + 1e-4 * np.abs(ref_lse)).all()
+    with pytest.raises(pkg.VerifyError):
+        bf = torch.zeros((1, 1, 128, 128), dtype=torch.bfloat16, device="cuda")
+        pkg.fused(bf, bf, bf, 0.1, q_descale=torch.ones((1, 1, 1), device="cuda"))
+
+
 def test_c4_sampled_rows(pkg, wl, oracle):
     """Full c4 size (bf16 causal B=1 H=32 N=16384 D=128): every output finite,
     sampled Q tiles of the first and last head against the oracle."""
