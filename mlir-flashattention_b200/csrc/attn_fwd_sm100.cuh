@@ -21,8 +21,11 @@
 //               (m, l) in registers, writes P (bf16 / f16 / e4m3) back into the
 //               S columns and rescales its O row in TMEM when m moved; at the
 //               end of a pair it writes O / l and the LSE.
+//   warps 10-11 idle (they complete warpgroup 2 for the register split).
 //   The two Q tiles ping-pong: while one softmax group works, the tensor
-//   cores run the other tile's GEMMs.
+//   cores run the other tile's GEMMs.  Registers: launched at 168 per thread
+//   (three warps share each SM sub-partition), the softmax warpgroups raise
+//   theirs to 224 and warpgroup 2 lowers its to 56 (setmaxnreg).
 //
 // TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,256+D)
 // O1 [256+D, 256+2D).  Exponentials are base 2 with the scale folded in:
@@ -106,7 +109,15 @@ struct FwdCfg {
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+// Register split (setmaxnreg): the two softmax warpgroups raise their limit
+// to kRegsSoftmax, warpgroup 2 (producer, MMA issuer, two idle warps) lowers
+// its own to kRegsOther.  The shares must fit in the registers the CTA is
+// launched with (kThreads x the kernel's register count), or the raise would
+// wait forever; the host checks the count before the first launch.
+constexpr int kRegsSoftmax = 224;
+constexpr int kRegsOther = 56;
+constexpr int kRegPool = 256 * kRegsSoftmax + 128 * kRegsOther;
 
 __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
 
@@ -256,202 +267,207 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tmap(&tmQ);
-      prefetch_tmap(&tmK);
-      prefetch_tmap(&tmV);
-      int ring = 0;  // K/V tiles issued so far (ring position)
-      int qi = 0;    // Q pairs issued so far
+  if (warp >= 8) {
+    setmaxnreg_dec<kRegsOther>();
+    if (warp == 8) {
+      // ------------------------------------------------------------ producer
+      if (lane == 0) {
+        prefetch_tmap(&tmQ);
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+        int ring = 0;  // K/V tiles issued so far (ring position)
+        int qi = 0;    // Q pairs issued so far
+        bool ok = true;
+        for (int r = 0; ok; ++r) {
+          const int w = item_index<CAUSAL>(r, cta, G, W);
+          if (w < 0) break;
+          const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
+          const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq, hk = h / p.group;
+          int n_t[2];
+          kv_counts<CAUSAL>(itm.pair, p.Nq, p.Nk, n_t);
+          const int nmax = max(n_t[0], n_t[1]);
+          // Q buffer: free once the previous pair's last S GEMMs completed.
+          if (!mbar_wait_bounded(q_empty, (static_cast<uint32_t>(qi) & 1u) ^ 1u, abort_flag,
+                                 p.status, kWaitLimitNs)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(q_full, 2 * C::kTileBytes);
+  #pragma unroll
+          for (int t = 0; t < 2; ++t)
+  #pragma unroll
+            for (int c = 0; c < C::kNBox; ++c)
+              tma_load_4d(sQ + t * C::kTileBytes + c * C::kBoxBytes, &tmQ, q_full,
+                          c * C::kBoxCols, itm.pair * 256 + 128 * t, h, b);
+          ++qi;
+          for (int j = 0; j < nmax && ok; ++j) {
+  #pragma unroll
+            for (int kv = 0; kv < 2; ++kv) {
+              const int s = ring % C::kStages;
+              const uint32_t u = static_cast<uint32_t>(ring / C::kStages);
+              if (!mbar_wait_bounded(&kv_empty[s], (u & 1u) ^ 1u, abort_flag, p.status,
+                                     kWaitLimitNs)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&kv_full[s], C::kTileBytes);
+  #pragma unroll
+              for (int c = 0; c < C::kNBox; ++c)
+                tma_load_4d(sKV + s * C::kTileBytes + c * C::kBoxBytes, kv ? &tmV : &tmK,
+                            &kv_full[s], c * C::kBoxCols, j * 128, hk, b);
+              ++ring;
+            }
+          }
+        }
+        // Wait for every copy this thread started before the CTA may exit.
+        if (qi > 0) drain_wait(q_full, static_cast<uint32_t>((qi - 1) & 1), p.status);
+        for (int s = 0; s < C::kStages; ++s) {
+          if (ring > s) {
+            const int armed = (ring - 1 - s) / C::kStages + 1;
+            drain_wait(&kv_full[s], static_cast<uint32_t>((armed - 1) & 1), p.status);
+          }
+        }
+      }
+      __syncwarp();
+    } else if (warp == 9) {
+      // ------------------------------------------------------------ MMA issuer
+      // The whole warp runs this schedule converged (waits by every lane, the
+      // MMA and commit instructions issued by one elected lane), so the
+      // descriptors below stay warp-uniform.
+      constexpr uint32_t idS = make_idesc(128, 128, C::kFmt, false);
+      constexpr uint32_t idO = make_idesc(128, D, C::kFmt, true);
+      // Descriptors of the first K step; later steps add (byte offset >> 4) to
+      // the 14-bit start-address field, which cannot carry (smem < 256 KB).
+      const uint64_t dQ0 = make_sdesc(smem_u32(sQ), 16, 1024);
+      const uint64_t dK0 = make_sdesc(smem_u32(sKV), 16, 1024);
+      const uint64_t dV0 = make_sdesc(smem_u32(sKV), C::kBoxBytes, 1024);
+      const uint32_t lead = elect_one();  // the lane that issues MMAs and commits
+      auto issue_S = [&](int t, int stage) {
+        const uint64_t a0 = dQ0 + static_cast<uint64_t>((t * C::kTileBytes) >> 4);
+        const uint64_t b0 = dK0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
+  #pragma unroll
+        for (int kk = 0; kk < C::kKStepsS; ++kk) {
+          constexpr int kBox = C::kBoxBytes;
+          const uint32_t off = ((kk * 32) / 128) * kBox + ((kk * 32) % 128);
+          mma_ss_lead<C::kKind>(lead, tmem + t * 128, a0 + (off >> 4), b0 + (off >> 4), idS,
+                                kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_PV = [&](int t, int stage, bool acc) {
+        const uint64_t b0 = dV0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
+  #pragma unroll
+        for (int kk = 0; kk < C::kKStepsPV; ++kk)
+          mma_ts_lead<C::kKind>(lead, tmem + 256 + t * D, tmem + t * 128 + kk * 8,
+                                b0 + static_cast<uint64_t>((kk * C::kKeysPerStep * 128) >> 4), idO,
+                                (acc || kk > 0) ? 1u : 0u);
+      };
+      auto wait = [&](uint64_t* bar, int phase) {
+        return warp_wait(bar, static_cast<uint32_t>(phase & 1), abort_flag, p.status);
+      };
+      int ring = 0;             // ring position of this pair's K_0
+      int qi = 0;               // pairs started
+      int pv_cnt[2] = {0, 0};   // P·V GEMMs committed per tile (pv_done phases)
+      int p_cnt[2] = {0, 0};    // p_ready phases consumed per tile
+      int items_t[2] = {0, 0};  // pairs in which tile t was active
       bool ok = true;
       for (int r = 0; ok; ++r) {
         const int w = item_index<CAUSAL>(r, cta, G, W);
         if (w < 0) break;
         const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
-        const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq, hk = h / p.group;
         int n_t[2];
         kv_counts<CAUSAL>(itm.pair, p.Nq, p.Nk, n_t);
         const int nmax = max(n_t[0], n_t[1]);
-        // Q buffer: free once the previous pair's last S GEMMs completed.
-        if (!mbar_wait_bounded(q_empty, (static_cast<uint32_t>(qi) & 1u) ^ 1u, abort_flag,
-                               p.status, kWaitLimitNs)) {
+        auto kst = [&](int j) { return (ring + 2 * j) % C::kStages; };
+        auto kph = [&](int j) { return (ring + 2 * j) / C::kStages; };
+        auto vst = [&](int j) { return (ring + 2 * j + 1) % C::kStages; };
+        auto vph = [&](int j) { return (ring + 2 * j + 1) / C::kStages; };
+        if (!wait(q_full, qi) || !wait(&kv_full[kst(0)], kph(0))) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(q_full, 2 * C::kTileBytes);
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-#pragma unroll
-          for (int c = 0; c < C::kNBox; ++c)
-            tma_load_4d(sQ + t * C::kTileBytes + c * C::kBoxBytes, &tmQ, q_full,
-                        c * C::kBoxCols, itm.pair * 256 + 128 * t, h, b);
-        ++qi;
+        tc_fence_after();
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (n_t[t] == 0) continue;
+          // S_t's columns hold the previous pair's last P_t until its P·V GEMM
+          // has completed.
+          if (pv_cnt[t] > 0 && !wait(&pv_done[t], pv_cnt[t] - 1)) {
+            ok = false;
+            break;
+          }
+          issue_S(t, kst(0));
+          mma_commit_lead(lead, &s_full[t]);
+        }
+        if (!ok) break;
+        mma_commit_lead(lead, &kv_empty[kst(0)]);        // K_0 free once both S GEMMs finish
+        if (nmax == 1) mma_commit_lead(lead, q_empty);  // every S GEMM of this pair is issued
+        // Per KV step j, for each Q tile t in turn: O_t += P_t(j)·V_j, then
+        // S_t(j+1) = Q_t·K_{j+1}ᵀ as soon as that P·V GEMM has finished reading
+        // P_t(j) (P lives in the S_t columns).  Tile t's next softmax then
+        // overlaps the other tile's GEMMs.
         for (int j = 0; j < nmax && ok; ++j) {
-#pragma unroll
-          for (int kv = 0; kv < 2; ++kv) {
-            const int s = ring % C::kStages;
-            const uint32_t u = static_cast<uint32_t>(ring / C::kStages);
-            if (!mbar_wait_bounded(&kv_empty[s], (u & 1u) ^ 1u, abort_flag, p.status,
-                                   kWaitLimitNs)) {
+          bool k_next = false;
+          if (!wait(&kv_full[vst(j)], vph(j))) {
+            ok = false;
+            break;
+          }
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= n_t[t]) continue;
+            if (!wait(&p_ready[t], p_cnt[t])) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&kv_full[s], C::kTileBytes);
-#pragma unroll
-            for (int c = 0; c < C::kNBox; ++c)
-              tma_load_4d(sKV + s * C::kTileBytes + c * C::kBoxBytes, kv ? &tmV : &tmK,
-                          &kv_full[s], c * C::kBoxCols, j * 128, hk, b);
-            ++ring;
-          }
-        }
-      }
-      // Wait for every copy this thread started before the CTA may exit.
-      if (qi > 0) drain_wait(q_full, static_cast<uint32_t>((qi - 1) & 1), p.status);
-      for (int s = 0; s < C::kStages; ++s) {
-        if (ring > s) {
-          const int armed = (ring - 1 - s) / C::kStages + 1;
-          drain_wait(&kv_full[s], static_cast<uint32_t>((armed - 1) & 1), p.status);
-        }
-      }
-    }
-    __syncwarp();
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
-    // The whole warp runs this schedule converged (waits by every lane, the
-    // MMA and commit instructions issued by one elected lane), so the
-    // descriptors below stay warp-uniform.
-    constexpr uint32_t idS = make_idesc(128, 128, C::kFmt, false);
-    constexpr uint32_t idO = make_idesc(128, D, C::kFmt, true);
-    // Descriptors of the first K step; later steps add (byte offset >> 4) to
-    // the 14-bit start-address field, which cannot carry (smem < 256 KB).
-    const uint64_t dQ0 = make_sdesc(smem_u32(sQ), 16, 1024);
-    const uint64_t dK0 = make_sdesc(smem_u32(sKV), 16, 1024);
-    const uint64_t dV0 = make_sdesc(smem_u32(sKV), C::kBoxBytes, 1024);
-    const uint32_t lead = elect_one();  // the lane that issues MMAs and commits
-    auto issue_S = [&](int t, int stage) {
-      const uint64_t a0 = dQ0 + static_cast<uint64_t>((t * C::kTileBytes) >> 4);
-      const uint64_t b0 = dK0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
-#pragma unroll
-      for (int kk = 0; kk < C::kKStepsS; ++kk) {
-        constexpr int kBox = C::kBoxBytes;
-        const uint32_t off = ((kk * 32) / 128) * kBox + ((kk * 32) % 128);
-        mma_ss_lead<C::kKind>(lead, tmem + t * 128, a0 + (off >> 4), b0 + (off >> 4), idS,
-                              kk > 0 ? 1u : 0u);
-      }
-    };
-    auto issue_PV = [&](int t, int stage, bool acc) {
-      const uint64_t b0 = dV0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
-#pragma unroll
-      for (int kk = 0; kk < C::kKStepsPV; ++kk)
-        mma_ts_lead<C::kKind>(lead, tmem + 256 + t * D, tmem + t * 128 + kk * 8,
-                              b0 + static_cast<uint64_t>((kk * C::kKeysPerStep * 128) >> 4), idO,
-                              (acc || kk > 0) ? 1u : 0u);
-    };
-    auto wait = [&](uint64_t* bar, int phase) {
-      return warp_wait(bar, static_cast<uint32_t>(phase & 1), abort_flag, p.status);
-    };
-    int ring = 0;             // ring position of this pair's K_0
-    int qi = 0;               // pairs started
-    int pv_cnt[2] = {0, 0};   // P·V GEMMs committed per tile (pv_done phases)
-    int p_cnt[2] = {0, 0};    // p_ready phases consumed per tile
-    int items_t[2] = {0, 0};  // pairs in which tile t was active
-    bool ok = true;
-    for (int r = 0; ok; ++r) {
-      const int w = item_index<CAUSAL>(r, cta, G, W);
-      if (w < 0) break;
-      const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
-      int n_t[2];
-      kv_counts<CAUSAL>(itm.pair, p.Nq, p.Nk, n_t);
-      const int nmax = max(n_t[0], n_t[1]);
-      auto kst = [&](int j) { return (ring + 2 * j) % C::kStages; };
-      auto kph = [&](int j) { return (ring + 2 * j) / C::kStages; };
-      auto vst = [&](int j) { return (ring + 2 * j + 1) % C::kStages; };
-      auto vph = [&](int j) { return (ring + 2 * j + 1) / C::kStages; };
-      if (!wait(q_full, qi) || !wait(&kv_full[kst(0)], kph(0))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      for (int t = 0; t < 2 && ok; ++t) {
-        if (n_t[t] == 0) continue;
-        // S_t's columns hold the previous pair's last P_t until its P·V GEMM
-        // has completed.
-        if (pv_cnt[t] > 0 && !wait(&pv_done[t], pv_cnt[t] - 1)) {
-          ok = false;
-          break;
-        }
-        issue_S(t, kst(0));
-        mma_commit_lead(lead, &s_full[t]);
-      }
-      if (!ok) break;
-      mma_commit_lead(lead, &kv_empty[kst(0)]);        // K_0 free once both S GEMMs finish
-      if (nmax == 1) mma_commit_lead(lead, q_empty);  // every S GEMM of this pair is issued
-      // Per KV step j, for each Q tile t in turn: O_t += P_t(j)·V_j, then
-      // S_t(j+1) = Q_t·K_{j+1}ᵀ as soon as that P·V GEMM has finished reading
-      // P_t(j) (P lives in the S_t columns).  Tile t's next softmax then
-      // overlaps the other tile's GEMMs.
-      for (int j = 0; j < nmax && ok; ++j) {
-        bool k_next = false;
-        if (!wait(&kv_full[vst(j)], vph(j))) {
-          ok = false;
-          break;
-        }
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (j >= n_t[t]) continue;
-          if (!wait(&p_ready[t], p_cnt[t])) {
-            ok = false;
-            break;
-          }
-          ++p_cnt[t];
-          // The first P·V GEMM of a pair overwrites O_t: the previous pair's
-          // epilogue must have read it.
-          if (j == 0 && items_t[t] > 0 && !wait(&o_free[t], items_t[t] - 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_PV(t, vst(j), j > 0);
-          mma_commit_lead(lead, &pv_done[t]);
-          ++pv_cnt[t];
-          if (j + 1 < n_t[t]) {
-            if (!k_next) {
-              if (!wait(&kv_full[kst(j + 1)], kph(j + 1))) {
-                ok = false;
-                break;
-              }
-              k_next = true;
-            }
-            if (!wait(&pv_done[t], pv_cnt[t] - 1)) {
+            ++p_cnt[t];
+            // The first P·V GEMM of a pair overwrites O_t: the previous pair's
+            // epilogue must have read it.
+            if (j == 0 && items_t[t] > 0 && !wait(&o_free[t], items_t[t] - 1)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_S(t, kst(j + 1));
-            mma_commit_lead(lead, &s_full[t]);
+            issue_PV(t, vst(j), j > 0);
+            mma_commit_lead(lead, &pv_done[t]);
+            ++pv_cnt[t];
+            if (j + 1 < n_t[t]) {
+              if (!k_next) {
+                if (!wait(&kv_full[kst(j + 1)], kph(j + 1))) {
+                  ok = false;
+                  break;
+                }
+                k_next = true;
+              }
+              if (!wait(&pv_done[t], pv_cnt[t] - 1)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_S(t, kst(j + 1));
+              mma_commit_lead(lead, &s_full[t]);
+            }
+          }
+          if (!ok) break;
+          mma_commit_lead(lead, &kv_empty[vst(j)]);  // V_j free once the P·V GEMMs finish
+          if (j + 1 < nmax) {
+            if (!k_next && !wait(&kv_full[kst(j + 1)], kph(j + 1))) {
+              ok = false;
+              break;
+            }
+            mma_commit_lead(lead, &kv_empty[kst(j + 1)]);  // K_{j+1} free once its S GEMMs finish
+            if (j + 2 == nmax) mma_commit_lead(lead, q_empty);
           }
         }
-        if (!ok) break;
-        mma_commit_lead(lead, &kv_empty[vst(j)]);  // V_j free once the P·V GEMMs finish
-        if (j + 1 < nmax) {
-          if (!k_next && !wait(&kv_full[kst(j + 1)], kph(j + 1))) {
-            ok = false;
-            break;
-          }
-          mma_commit_lead(lead, &kv_empty[kst(j + 1)]);  // K_{j+1} free once its S GEMMs finish
-          if (j + 2 == nmax) mma_commit_lead(lead, q_empty);
-        }
+        for (int t = 0; t < 2; ++t)
+          if (n_t[t] > 0) ++items_t[t];
+        ring += 2 * nmax;
+        ++qi;
       }
-      for (int t = 0; t < 2; ++t)
-        if (n_t[t] > 0) ++items_t[t];
-      ring += 2 * nmax;
-      ++qi;
+      // Drain every MMA this warp issued before TMEM is released.
+      mma_commit_lead(lead, drain);
+      if (lane == 0) drain_wait(drain, 0, p.status);
+      __syncwarp();
     }
-    // Drain every MMA this warp issued before TMEM is released.
-    mma_commit_lead(lead, drain);
-    if (lane == 0) drain_wait(drain, 0, p.status);
-    __syncwarp();
+    // Warps 10 and 11 only complete warpgroup 2 for the register split.
   } else {
+    setmaxnreg_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax
     const int t = warp >> 2;  // Q tile of this warpgroup
     const int quarter = warp & 3;

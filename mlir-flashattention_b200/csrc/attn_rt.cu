@@ -180,11 +180,21 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
   auto kern = attn_sm100::attn_fwd_sm100_kernel<D, MODE, ELT>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
+  static int launch_regs = 0;
   std::call_once(once, [&] {
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(C::kSmemBytes));
+    cudaFuncAttributes fa{};
+    if (attr_err == cudaSuccess) attr_err = cudaFuncGetAttributes(&fa, kern);
+    launch_regs = fa.numRegs;
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute");
+  // The kernel re-divides its registers between warpgroups (setmaxnreg); a
+  // build whose launch register count cannot cover the split must not run.
+  if (launch_regs * attn_sm100::kThreads < attn_sm100::kRegPool)
+    return fail(ATTN_ERR_UNSUPPORTED,
+                "kernel built with %d registers per thread; the register split needs %d",
+                launch_regs, attn_sm100::kRegPool / attn_sm100::kThreads);
   const CUtensorMapDataType dt =
       FP8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
           : (ELT == attn_sm100::kEltF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16

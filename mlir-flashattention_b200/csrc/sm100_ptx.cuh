@@ -225,6 +225,16 @@ __host__ __device__ constexpr uint32_t make_idesc(int M, int N, uint32_t fmt, bo
 // tcgen05.ld / st, 32 lanes x 32 bits shape: thread i of the warp accesses
 // TMEM lane (warp's lane quarter base + i), columns [col, col + N).
 // ---------------------------------------------------------------------------
+// Per-warpgroup register limits (all four warps of a warpgroup execute it).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
