@@ -62,6 +62,10 @@ __global__ void __launch_bounds__(kRows * 32)
 #pragma unroll
   for (int i = 0; i < NO; ++i) o[i] = 0.f;
   float m = -INFINITY, l = 0.f;
+  // Dense masks: a row masked over all of keys [0, 128) (the reference's
+  // first KV tile) is NaN in the reference, whose loop evaluates
+  // exp(-inf - -inf) there (TilingPass.cpp:291-305).
+  bool seen_first_tile = p.mask_kind != 2;
 
   int kend = p.Nk;
   if (p.mask_kind == 1) {
@@ -88,6 +92,7 @@ __global__ void __launch_bounds__(kRows * 32)
     if (p.mask_kind == 2 && live && key < p.Nk)
       masked = masked || p.mask[b * p.m_sb + h * p.m_sh + row * p.m_sn + key] != 0;
     if (masked) s = -INFINITY;
+    if (k0 < 128) seen_first_tile |= __any_sync(0xffffffffu, !masked);
     float mx = s;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -112,13 +117,15 @@ __global__ void __launch_bounds__(kRows * 32)
     m = m_new;
   }
   if (live) {
+    const float nan = __int_as_float(0x7fc00000);
     float* O = p.o + b * p.o_sb + h * p.o_sh + row * p.o_sn;
 #pragma unroll
     for (int i = 0; i < NO; ++i) {
       const int d = lane + 32 * i;
-      if (d < D) O[d] = o[i] / l;
+      if (d < D) O[d] = seen_first_tile ? o[i] / l : nan;
     }
-    if (p.lse && lane == 0) p.lse[static_cast<int64_t>(bh) * p.Nq + row] = m + logf(l);
+    if (p.lse && lane == 0)
+      p.lse[static_cast<int64_t>(bh) * p.Nq + row] = seen_first_tile ? m + logf(l) : nan;
   }
 }
 

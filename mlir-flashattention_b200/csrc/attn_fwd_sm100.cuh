@@ -506,6 +506,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           kd_cur = __ldg(kd_row);
         }
       }
+      // Dense masks: the reference's loop (TilingPass.cpp:291-305) evaluates
+      // exp(-inf - -inf) = NaN when a row is masked over its whole first KV
+      // tile, and that NaN reaches O; such rows are NaN here too.
+      bool nan_row = false;
       const uint8_t* mrow = nullptr;
       if constexpr (DENSE)
         mrow = p.mask + b * p.m_sb + h * p.m_sh + static_cast<int64_t>(min(row, p.Nq - 1)) * p.m_sn;
@@ -570,6 +574,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             a1 = min3(a1, s[c + 2], s[c + 3]);
           }
           red = min3(a0, a1, fminf(s[126], s[127]));
+        }
+        if constexpr (DENSE) {
+          if (j == 0) nan_row = red == mask_val;
         }
         const float m_cand = red * sl2;
         float alpha = 1.f;
@@ -637,7 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const float inv_l = p.o_scale * vd / l;
+      const float inv_l = nan_row ? __int_as_float(0x7fc00000) : p.o_scale * vd / l;
       const int64_t obase = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
                             static_cast<int64_t>(row) * p.o_sn;
       const bool live = row < p.Nq;
@@ -681,7 +688,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (live && p.lse)
         p.lse[static_cast<int64_t>(itm.bh) * p.Nq + row] =
-            (m + __log2f(l)) * 0.69314718055994531f;
+            nan_row ? __int_as_float(0x7fc00000) : (m + __log2f(l)) * 0.69314718055994531f;
     }
   }
 

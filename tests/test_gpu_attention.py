@@ -49,7 +49,9 @@ def test_f32_dense_mask_rank2_memref(pkg, wl, oracle):
     Nq, Nk, D = 96, 160, 32
     Q, K, V = (rng.standard_normal((n, D)).astype(np.float32) for n in (Nq, Nk, Nk))
     M = rng.random((Nq, Nk)) < 0.3
-    M[:, 0] = False  # keep every row partly visible
+    M[:, 0] = False
+    M[[3, 40], :128] = True  # masked over the whole first KV tile, visible later
+    M[60, :] = True          # masked everywhere
     ref, _ = oracle.attn_fused_f32(Q, K, V, 0.2, mask=M)
     tq, tk, tv = (torch.from_numpy(a) for a in (Q, K, V))
     tm = torch.from_numpy(M.astype(np.uint8))
@@ -58,7 +60,12 @@ def test_f32_dense_mask_rank2_memref(pkg, wl, oracle):
     rc = L._mlir_ciface_attn_fused_f32_mask(pkg.memref(tq), pkg.memref(tk), pkg.memref(tv), 0.2,
                                             pkg.memref(tm), pkg.memref(to))
     assert rc == 0, pkg.last_error()
-    assert _rel(to.numpy(), ref) <= 1e-4
+    got = to.numpy()
+    # The reference's loop yields NaN for rows masked over their first KV tile.
+    nan_rows = np.isnan(ref).all(axis=1)
+    assert nan_rows.tolist() == [r in (3, 40, 60) for r in range(Nq)]
+    assert (np.isnan(got) == np.isnan(ref)).all()
+    assert _rel(got[~nan_rows], ref[~nan_rows]) <= 1e-4
 
 
 @pytest.mark.parametrize("D", [64, 128])
@@ -213,14 +220,23 @@ def test_bf16_dense_mask_parity(pkg, wl, oracle, D):
     inp = wl.make_inputs(w)
     rng = np.random.default_rng(D)
     M = rng.random((2, 3, 1000, 1000)) < 0.35
-    M[..., 0] = False  # a row masked over a whole first tile is NaN in the reference
+    M[..., 0] = False
+    # Rows masked over their whole first KV tile (keys 0-127) are NaN in the
+    # reference (exp(-inf - -inf) in its loop), whatever later keys allow.
+    M[0, 1, [5, 131, 700], :128] = True
+    M[1, 2, 999, :] = True
     q, k, v = wl.to_device(inp, w)
     L = torch.empty((2, 3, 1000), dtype=torch.float32, device="cuda")
     out = pkg.fused(q, k, v, w.scale, mask=torch.from_numpy(M).cuda(), lse=L)
     pkg.check_status(0)
     ref, ref_lse = oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale, mask=M)
-    assert _rel(out.float().cpu().numpy(), ref) <= 2e-2
-    assert np.abs(L.cpu().numpy() - ref_lse).max() <= 1e-3
+    got, lse = out.float().cpu().numpy(), L.cpu().numpy()
+    nan_rows = np.isnan(ref).all(axis=-1)
+    assert nan_rows.sum() == 4 and nan_rows[0, 1, [5, 131, 700]].all() and nan_rows[1, 2, 999]
+    assert (np.isnan(got) == np.isnan(ref)).all()
+    assert (np.isnan(lse) == np.isnan(ref_lse)).all()
+    assert _rel(got[~nan_rows], ref[~nan_rows]) <= 2e-2
+    assert np.abs(lse[~nan_rows] - ref_lse[~nan_rows]).max() <= 1e-3
 
 
 def test_dense_causal_mask_equals_causal_variant(pkg, wl):
