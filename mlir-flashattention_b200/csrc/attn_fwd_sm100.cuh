@@ -73,7 +73,18 @@ struct FwdParams {
   const float* kd_blk;
   const float* vd_head;
   int nqb, nkb;
+  // Dense mode: class of every (mask slice, Q tile, KV tile) block of the
+  // mask (kTileFull / kTilePartial / kTileEmpty, see classify_mask_tiles);
+  // byte strides per batch and head (0 for a broadcast mask), rows of nkt.
+  const uint8_t* tile_cls;
+  int64_t cls_sb, cls_sh;
+  int nkt;
 };
+
+// Classes of a 128 x 128 block of a dense mask (rows < Nq, keys < Nk).
+constexpr uint8_t kTileFull = 0;     // nothing masked: no per-element select
+constexpr uint8_t kTilePartial = 1;  // some masked, or keys past Nk
+constexpr uint8_t kTileEmpty = 2;    // everything masked: never loaded or multiplied
 
 // Mask modes of the kernel (compile-time specialisations).
 constexpr int kMaskNone = 0;    // no mask operand
@@ -183,6 +194,81 @@ __device__ __forceinline__ void kv_counts(int pair, int Nq, int Nk, int (&n_t)[2
   }
 }
 
+// The KV tiles one pair visits: the union, in increasing order, of the KV
+// tiles either Q tile needs, and which tile needs which.  No-mask and causal
+// pairs need a prefix per tile (kv_counts).  Dense-mask pairs skip KV tiles
+// whose mask block is empty for a Q tile (the FULL / MASKED / BOUNDARY split
+// of the reference design, Design.md:412-419, applied to an arbitrary mask);
+// a Q tile whose first KV tile is empty needs none: its rows are NaN, as in
+// the reference (see the softmax).
+template <int MODE>
+struct PairSched {
+  int n_t[2];             // prefix lengths (no-mask, causal)
+  const uint8_t* cls[2];  // dense: the Q tiles' class rows (nullptr: no KV tile)
+  int nkt;                // dense: KV tiles per row
+
+  __device__ __forceinline__ bool act(int t, int kt) const {
+    if constexpr (MODE == kMaskDense)
+      return cls[t] != nullptr && __ldg(cls[t] + kt) != kTileEmpty;
+    else
+      return kt < n_t[t];
+  }
+  __device__ __forceinline__ bool any(int t) const {
+    if constexpr (MODE == kMaskDense) return cls[t] != nullptr;
+    else return n_t[t] > 0;
+  }
+  __device__ __forceinline__ int end() const {
+    if constexpr (MODE == kMaskDense) return nkt;
+    else return max(n_t[0], n_t[1]);
+  }
+  // Next KV tile of the union after kt (end() if none).
+  __device__ __forceinline__ int next(int kt) const {
+    if constexpr (MODE == kMaskDense) {
+      for (++kt; kt < nkt; ++kt)
+        if (act(0, kt) || act(1, kt)) break;
+      return kt;
+    } else {
+      return kt + 1;
+    }
+  }
+  // Next KV tile Q tile t needs after kt (end() if none).
+  __device__ __forceinline__ int next_t(int t, int kt) const {
+    if constexpr (MODE == kMaskDense) {
+      for (++kt; kt < nkt; ++kt)
+        if (act(t, kt)) break;
+      return kt;
+    } else {
+      return kt + 1 < n_t[t] ? kt + 1 : end();
+    }
+  }
+  __device__ __forceinline__ bool full(int t, int kt) const {
+    if constexpr (MODE == kMaskDense) return __ldg(cls[t] + kt) == kTileFull;
+    else return false;
+  }
+};
+
+template <int MODE>
+__device__ __forceinline__ PairSched<MODE> make_sched(const Item& itm, const FwdParams& p) {
+  PairSched<MODE> sc;
+  if constexpr (MODE == kMaskDense) {
+    const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq;
+    sc.nkt = p.nkt;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int qt = itm.pair * 2 + t;
+      const uint8_t* row = p.tile_cls + b * p.cls_sb + h * p.cls_sh +
+                           static_cast<int64_t>(qt) * p.nkt;
+      sc.cls[t] = (qt * 128 < p.Nq && __ldg(row) != kTileEmpty) ? row : nullptr;
+      sc.n_t[t] = 0;
+    }
+  } else {
+    kv_counts<MODE == kMaskCausal>(itm.pair, p.Nq, p.Nk, sc.n_t);
+    sc.cls[0] = sc.cls[1] = nullptr;
+    sc.nkt = 0;
+  }
+  return sc;
+}
+
 // 128 mask bytes of one row for keys [kbase, kbase+128): bit c of the
 // returned words is set when key kbase+c is masked or does not exist.
 __device__ __forceinline__ void load_mask_row(const uint8_t* mrow, int kbase, int Nk, bool vec,
@@ -283,9 +369,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (w < 0) break;
           const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
           const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq, hk = h / p.group;
-          int n_t[2];
-          kv_counts<CAUSAL>(itm.pair, p.Nq, p.Nk, n_t);
-          const int nmax = max(n_t[0], n_t[1]);
+          const PairSched<MODE> sc = make_sched<MODE>(itm, p);
+          const int kt_end = sc.end();
+          int kt = sc.next(-1);
+          if (kt >= kt_end) continue;  // no KV tile at all (dense: every row NaN)
           // Q buffer: free once the previous pair's last S GEMMs completed.
           if (!mbar_wait_bounded(q_empty, (static_cast<uint32_t>(qi) & 1u) ^ 1u, abort_flag,
                                  p.status, kWaitLimitNs)) {
@@ -300,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_4d(sQ + t * C::kTileBytes + c * C::kBoxBytes, &tmQ, q_full,
                           c * C::kBoxCols, itm.pair * 256 + 128 * t, h, b);
           ++qi;
-          for (int j = 0; j < nmax && ok; ++j) {
+          for (; kt < kt_end && ok; kt = sc.next(kt)) {
   #pragma unroll
             for (int kv = 0; kv < 2; ++kv) {
               const int s = ring % C::kStages;
@@ -314,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   #pragma unroll
               for (int c = 0; c < C::kNBox; ++c)
                 tma_load_4d(sKV + s * C::kTileBytes + c * C::kBoxBytes, kv ? &tmV : &tmK,
-                            &kv_full[s], c * C::kBoxCols, j * 128, hk, b);
+                            &kv_full[s], c * C::kBoxCols, kt * 128, hk, b);
               ++ring;
             }
           }
@@ -374,20 +461,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int w = item_index<CAUSAL>(r, cta, G, W);
         if (w < 0) break;
         const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
-        int n_t[2];
-        kv_counts<CAUSAL>(itm.pair, p.Nq, p.Nk, n_t);
-        const int nmax = max(n_t[0], n_t[1]);
-        auto kst = [&](int j) { return (ring + 2 * j) % C::kStages; };
-        auto kph = [&](int j) { return (ring + 2 * j) / C::kStages; };
-        auto vst = [&](int j) { return (ring + 2 * j + 1) % C::kStages; };
-        auto vph = [&](int j) { return (ring + 2 * j + 1) / C::kStages; };
+        const PairSched<MODE> sc = make_sched<MODE>(itm, p);
+        const int kt_end = sc.end();
+        const int kt0 = sc.next(-1);
+        if (kt0 >= kt_end) continue;  // no KV tile (the producer skips the pair too)
+        // Ring slots of the i-th KV tile of this pair (K, then V).
+        auto kst = [&](int i) { return (ring + 2 * i) % C::kStages; };
+        auto kph = [&](int i) { return (ring + 2 * i) / C::kStages; };
+        auto vst = [&](int i) { return (ring + 2 * i + 1) % C::kStages; };
+        auto vph = [&](int i) { return (ring + 2 * i + 1) / C::kStages; };
         if (!wait(q_full, qi) || !wait(&kv_full[kst(0)], kph(0))) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int t = 0; t < 2 && ok; ++t) {
-          if (n_t[t] == 0) continue;
+          if (!sc.act(t, kt0)) continue;
           // S_t's columns hold the previous pair's last P_t until its P·V GEMM
           // has completed.
           if (pv_cnt[t] > 0 && !wait(&pv_done[t], pv_cnt[t] - 1)) {
@@ -398,20 +487,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit_lead(lead, &s_full[t]);
         }
         if (!ok) break;
-        mma_commit_lead(lead, &kv_empty[kst(0)]);        // K_0 free once both S GEMMs finish
-        if (nmax == 1) mma_commit_lead(lead, q_empty);  // every S GEMM of this pair is issued
-        // Per KV step j, for each Q tile t in turn: O_t += P_t(j)·V_j, then
-        // S_t(j+1) = Q_t·K_{j+1}ᵀ as soon as that P·V GEMM has finished reading
-        // P_t(j) (P lives in the S_t columns).  Tile t's next softmax then
-        // overlaps the other tile's GEMMs.
-        for (int j = 0; j < nmax && ok; ++j) {
+        mma_commit_lead(lead, &kv_empty[kst(0)]);  // K free once its S GEMMs finish
+        if (sc.next(kt0) >= kt_end) mma_commit_lead(lead, q_empty);  // all S GEMMs issued
+        // Per KV tile, for each Q tile t that needs it: O_t += P_t·V, then
+        // S_t = Q_t·Kᵀ of t's next KV tile as soon as that P·V GEMM has
+        // finished reading P_t (P lives in the S_t columns).  Tile t's next
+        // softmax then overlaps the other tile's GEMMs.
+        bool first_pv[2] = {true, true};
+        int i = 0;  // position of kt in this pair's KV tile list
+        for (int kt = kt0; kt < kt_end && ok; ++i) {
+          const int kn = sc.next(kt);
           bool k_next = false;
-          if (!wait(&kv_full[vst(j)], vph(j))) {
+          auto wait_k_next = [&]() {
+            if (!k_next) k_next = wait(&kv_full[kst(i + 1)], kph(i + 1));
+            return k_next;
+          };
+          if (!wait(&kv_full[vst(i)], vph(i))) {
             ok = false;
             break;
           }
           for (int t = 0; t < 2 && ok; ++t) {
-            if (j >= n_t[t]) continue;
+            if (!sc.act(t, kt)) continue;
             if (!wait(&p_ready[t], p_cnt[t])) {
               ok = false;
               break;
@@ -419,45 +515,54 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++p_cnt[t];
             // The first P·V GEMM of a pair overwrites O_t: the previous pair's
             // epilogue must have read it.
-            if (j == 0 && items_t[t] > 0 && !wait(&o_free[t], items_t[t] - 1)) {
+            if (first_pv[t] && items_t[t] > 0 && !wait(&o_free[t], items_t[t] - 1)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_PV(t, vst(j), j > 0);
+            issue_PV(t, vst(i), !first_pv[t]);
+            first_pv[t] = false;
             mma_commit_lead(lead, &pv_done[t]);
             ++pv_cnt[t];
-            if (j + 1 < n_t[t]) {
-              if (!k_next) {
-                if (!wait(&kv_full[kst(j + 1)], kph(j + 1))) {
-                  ok = false;
-                  break;
-                }
-                k_next = true;
-              }
-              if (!wait(&pv_done[t], pv_cnt[t] - 1)) {
+            if (kn < kt_end && sc.act(t, kn)) {
+              if (!wait_k_next() || !wait(&pv_done[t], pv_cnt[t] - 1)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              issue_S(t, kst(j + 1));
+              issue_S(t, kst(i + 1));
               mma_commit_lead(lead, &s_full[t]);
             }
           }
           if (!ok) break;
-          mma_commit_lead(lead, &kv_empty[vst(j)]);  // V_j free once the P·V GEMMs finish
-          if (j + 1 < nmax) {
-            if (!k_next && !wait(&kv_full[kst(j + 1)], kph(j + 1))) {
+          if constexpr (DENSE) {
+            // A Q tile that skipped kt but needs kn gets its S GEMM here.
+            for (int t = 0; t < 2 && ok; ++t) {
+              if (kn >= kt_end || sc.act(t, kt) || !sc.act(t, kn)) continue;
+              if (!wait_k_next() || (pv_cnt[t] > 0 && !wait(&pv_done[t], pv_cnt[t] - 1))) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_S(t, kst(i + 1));
+              mma_commit_lead(lead, &s_full[t]);
+            }
+            if (!ok) break;
+          }
+          mma_commit_lead(lead, &kv_empty[vst(i)]);  // V free once the P·V GEMMs finish
+          if (kn < kt_end) {
+            if (!wait_k_next()) {
               ok = false;
               break;
             }
-            mma_commit_lead(lead, &kv_empty[kst(j + 1)]);  // K_{j+1} free once its S GEMMs finish
-            if (j + 2 == nmax) mma_commit_lead(lead, q_empty);
+            mma_commit_lead(lead, &kv_empty[kst(i + 1)]);  // K free once its S GEMMs finish
+            if (sc.next(kn) >= kt_end) mma_commit_lead(lead, q_empty);
           }
+          kt = kn;
         }
         for (int t = 0; t < 2; ++t)
-          if (n_t[t] > 0) ++items_t[t];
-        ring += 2 * nmax;
+          if (sc.any(t)) ++items_t[t];
+        ring += 2 * i;
         ++qi;
       }
       // Drain every MMA this warp issued before TMEM is released.
@@ -484,13 +589,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int w = item_index<CAUSAL>(rr, cta, G, W);
       if (w < 0) break;
       const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
-      int n_t[2];
-      kv_counts<CAUSAL>(itm.pair, p.Nq, p.Nk, n_t);
-      const int n = n_t[t];
-      if (n == 0) continue;
+      const PairSched<MODE> sc = make_sched<MODE>(itm, p);
       const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq;
       const int qs = itm.pair * 256 + 128 * t;
       const int row = qs + r;
+      if (!sc.any(t)) {
+        if constexpr (DENSE) {
+          // Every row of this Q tile is masked over its first KV tile: NaN,
+          // as in the reference (see nan_row below); no GEMM is involved.
+          if (qs < p.Nq && row < p.Nq) {
+            const int64_t obase = static_cast<int64_t>(b) * p.o_sb +
+                                  static_cast<int64_t>(h) * p.o_sh +
+                                  static_cast<int64_t>(row) * p.o_sn;
+            const float nan = __int_as_float(0x7fc00000);
+            if (p.out_kind == 1) {
+              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + obase);
+#pragma unroll
+              for (int i = 0; i < D / 4; ++i) dst[i] = make_float4(nan, nan, nan, nan);
+            } else {
+              const uint32_t q = p.out_kind == 2 ? 0x7e007e00u : 0x7fc07fc0u;
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.o) + obase);
+#pragma unroll
+              for (int i = 0; i < D / 8; ++i) dst[i] = make_uint4(q, q, q, q);
+            }
+            if (p.lse) p.lse[static_cast<int64_t>(itm.bh) * p.Nq + row] = nan;
+          }
+        }
+        continue;
+      }
+      const int kt_end = sc.end();
       float m = -INFINITY;
       float l = 0.f;
       // e4m3 per-block factors: the Q block's folds into this tile's exponent
@@ -513,9 +640,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t* mrow = nullptr;
       if constexpr (DENSE)
         mrow = p.mask + b * p.m_sb + h * p.m_sh + static_cast<int64_t>(min(row, p.Nq - 1)) * p.m_sn;
-      for (int j = 0; j < n; ++j, ++steps) {
+      bool first = true;
+      for (int kt = 0; kt < kt_end; ++steps) {
+        const int kn = sc.next_t(t, kt);
+        // Dense: mask bits only for partial blocks (full ones mask nothing).
+        const bool sel = DENSE && !sc.full(t, kt);
         uint32_t mbits[4];
-        if constexpr (DENSE) load_mask_row(mrow, j * 128, p.Nk, p.mask_vec != 0, mbits);
+        if constexpr (DENSE) {
+          if (sel) load_mask_row(mrow, kt * 128, p.Nk, p.mask_vec != 0, mbits);
+        }
         if (!warp_wait(&s_full[t], static_cast<uint32_t>(steps & 1), abort_flag, p.status)) {
           ok = false;
           break;
@@ -525,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (FP8) {
           if (kd_row) {
             sl2 *= kd_cur;
-            if (j + 1 < n) kd_cur = __ldg(kd_row + j + 1);  // next step's, loaded early
+            if (kn < kt_end) kd_cur = __ldg(kd_row + kn);  // next step's, loaded early
           }
         }
         float s[128];
@@ -544,11 +677,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             s[96 + i] = __uint_as_float(r3[i]);
           }
         }
-        const int kbase = j * 128;
+        const int kbase = kt * 128;
         if constexpr (DENSE) {
+          if (sel) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
-            if ((mbits[c >> 5] >> (c & 31)) & 1u) s[c] = mask_val;
+            for (int c = 0; c < 128; ++c)
+              if ((mbits[c >> 5] >> (c & 31)) & 1u) s[c] = mask_val;
+          }
         }
         const bool edge = !DENSE && ((kbase + 128 > p.Nk) || (CAUSAL && kbase + 127 > qs));
         if (edge) {
@@ -576,7 +711,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           red = min3(a0, a1, fminf(s[126], s[127]));
         }
         if constexpr (DENSE) {
-          if (j == 0) nan_row = red == mask_val;
+          if (kt == 0) nan_row = red == mask_val;
         }
         const float m_cand = red * sl2;
         float alpha = 1.f;
@@ -619,7 +754,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float q0, q1;
         f2_unpack(f2_add(acc0, acc1), q0, q1);
         l = l * alpha + (q0 + q1);
-        const bool need = (j > 0) && (alpha != 1.f);
+        const bool need = !first && (alpha != 1.f);
+        first = false;
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
@@ -635,6 +771,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_ready[t]);
+        kt = kn;
       }
       if (!ok) break;
       // -------------------------------------------------------- epilogue
@@ -698,6 +835,56 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// Classes of the 128 x 128 blocks of a dense mask, for the dense mode's KV
+// tile skipping.  One CTA per (mask slice, Q tile), thread r owning mask row
+// 128·qt + r; per KV tile the CTA ORs "some key visible" and "some key masked"
+// over its rows (rows >= Nq ignored) and writes kTileEmpty, kTilePartial
+// (also every tile reaching past Nk) or kTileFull.  Reads each distinct mask
+// slice once: HBM-bound, Nq·Nk bytes per slice.
+__global__ void __launch_bounds__(128)
+    classify_mask_tiles(const uint8_t* __restrict__ mask, int64_t m_sb, int64_t m_sh,
+                        int64_t m_sn, int Hm, int nqt, int Nq, int Nk, int nkt, int vec,
+                        uint8_t* __restrict__ cls) {
+  const int qt = static_cast<int>(blockIdx.x % static_cast<unsigned>(nqt));
+  const int slice = static_cast<int>(blockIdx.x / static_cast<unsigned>(nqt));
+  const int bm = slice / Hm, hm = slice - (slice / Hm) * Hm;
+  const int row = qt * 128 + static_cast<int>(threadIdx.x);
+  const bool live = row < Nq;
+  const uint8_t* mrow = mask + bm * m_sb + hm * m_sh + static_cast<int64_t>(min(row, Nq - 1)) * m_sn;
+  uint8_t* out = cls + static_cast<int64_t>(blockIdx.x) * nkt;
+  for (int kt = 0; kt < nkt; ++kt) {
+    const int kbase = kt * 128;
+    bool vis = false, msk = false;
+    if (live) {
+      if (vec && kbase + 128 <= Nk) {
+        const uint4* src = reinterpret_cast<const uint4*>(mrow + kbase);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 v = __ldg(src + q);
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            msk |= w[e] != 0u;
+            vis |= ((w[e] - 0x01010101u) & ~w[e] & 0x80808080u) != 0u;  // some byte is 0
+          }
+        }
+      } else {
+        const int lim = min(128, Nk - kbase);
+        for (int c = 0; c < lim; ++c) {
+          const bool m = mrow[kbase + c] != 0;
+          msk |= m;
+          vis |= !m;
+        }
+      }
+    }
+    const int any_vis = __syncthreads_or(vis);
+    const int any_msk = __syncthreads_or(msk);
+    if (threadIdx.x == 0)
+      out[kt] = !any_vis ? kTileEmpty
+                         : ((any_msk || kbase + 128 > Nk) ? kTilePartial : kTileFull);
   }
 }
 

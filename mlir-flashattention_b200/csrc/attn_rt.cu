@@ -248,14 +248,46 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
     p.mask_vec = rows_aligned ? 1 : 0;
   }
   p.num_bh = static_cast<int>(d.B * d.Hq);
+  // Dense masks: classify the mask's 128 x 128 blocks first (stream-ordered
+  // scratch, freed after the attention kernel) so that fully masked KV tiles
+  // are skipped and unmasked ones need no per-element select.
+  uint8_t* cls = nullptr;
+  if (MODE == attn_sm100::kMaskDense) {
+    const int64_t nqt = (d.Nq + 127) / 128, nkt = (d.Nk + 127) / 128;
+    const int64_t Bm = (d.B == 1 || d.mask_stride[0] == 0) ? 1 : d.B;
+    const int64_t Hm = (d.Hq == 1 || d.mask_stride[1] == 0) ? 1 : d.Hq;
+    const int64_t blocks = Bm * Hm * nqt;
+    if (blocks >= (1ll << 31)) return fail(ATTN_ERR_SHAPE, "dense mask too large to classify");
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&cls),
+                                    static_cast<size_t>(blocks * nkt), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync (mask tile classes)");
+    attn_sm100::classify_mask_tiles<<<static_cast<unsigned>(blocks), 128, 0, stream>>>(
+        d.mask, Bm == 1 ? 0 : d.mask_stride[0], Hm == 1 ? 0 : d.mask_stride[1], d.mask_stride[2],
+        static_cast<int>(Hm), static_cast<int>(nqt), static_cast<int>(d.Nq),
+        static_cast<int>(d.Nk), static_cast<int>(nkt), p.mask_vec, cls);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      cudaFreeAsync(cls, stream);
+      return cuda_fail(e, "classify_mask_tiles launch");
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    p.tile_cls = cls;
+    p.cls_sb = Bm == 1 ? 0 : Hm * nqt * nkt;
+    p.cls_sh = Hm == 1 ? 0 : nqt * nkt;
+    p.nkt = static_cast<int>(nkt);
+  }
   // Persistent launch: one CTA per SM (TMEM and shared memory allow one),
   // each walking its share of the (slice, Q-tile pair) work list.
   int sms = 0;
-  if ((rc = sm_count(&sms)) != ATTN_OK) return rc;
+  if ((rc = sm_count(&sms)) != ATTN_OK) {
+    if (cls) cudaFreeAsync(cls, stream);
+    return rc;
+  }
   const int64_t items = static_cast<int64_t>(p.num_bh) * p.num_pairs;
   dim3 grid(static_cast<unsigned>(std::min<int64_t>(items, sms)));
   kern<<<grid, attn_sm100::kThreads, C::kSmemBytes, stream>>>(mq, mk, mv, p);
   cudaError_t e = cudaGetLastError();
+  if (cls) cudaFreeAsync(cls, stream);
   if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_sm100 launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return ATTN_OK;

@@ -239,6 +239,53 @@ def test_bf16_dense_mask_parity(pkg, wl, oracle, D):
     assert np.abs(lse[~nan_rows] - ref_lse[~nan_rows]).max() <= 1e-3
 
 
+@pytest.mark.parametrize("D,broadcast", [(128, False), (64, False), (128, True)])
+def test_bf16_dense_block_sparse_mask(pkg, wl, oracle, D, broadcast):
+    """Block-structured masks: 128 x 128 blocks fully visible, fully masked
+    (skipped by the kernel) or mixed, with ragged Nq / Nk and Q tiles whose
+    first KV tile is fully masked (NaN rows, as in the reference)."""
+    B, H, Nq, Nk = 2, 3, 700, 900
+    w = wl.Workload("t", "bf16", B, H, H, Nq, D, False, seed=60 + D)
+    inp = wl.make_inputs(w)
+    rng = np.random.default_rng(D + broadcast)
+    k_in = rng.standard_normal((B, H, Nk, D)).astype(np.float32)
+    v_in = rng.standard_normal((B, H, Nk, D)).astype(np.float32)
+    kf, vf = wl.round_bf16(k_in), wl.round_bf16(v_in)
+    nqt, nkt = -(-Nq // 128), -(-Nk // 128)
+    shape = (1, 1) if broadcast else (B, H)
+    kind = rng.choice(3, size=shape + (nqt, nkt), p=[0.4, 0.35, 0.25])  # full, empty, mixed
+    kind[..., 2, 0] = 1                      # a Q tile whose first KV tile is masked: NaN rows
+    kind[..., 3, :] = 1                      # a Q tile masked everywhere
+    kind[..., 4, 0] = 0
+    M = np.zeros(shape + (nqt * 128, nkt * 128), bool)
+    for idx in np.ndindex(*kind.shape):
+        r0, c0 = idx[-2] * 128, idx[-1] * 128
+        blk = M[idx[:-2]][r0:r0 + 128, c0:c0 + 128]
+        if kind[idx] == 1:
+            blk[:] = True
+        elif kind[idx] == 2:
+            blk[:] = rng.random((128, 128)) < 0.4
+    M = M[..., :Nq, :Nk]
+    q = torch.from_numpy(inp.qf).to(torch.bfloat16).cuda()
+    k = torch.from_numpy(kf).to(torch.bfloat16).cuda()
+    v = torch.from_numpy(vf).to(torch.bfloat16).cuda()
+    tm = torch.from_numpy(np.ascontiguousarray(M)).cuda()
+    if broadcast:
+        tm = tm.reshape(Nq, Nk)
+    L = torch.empty((B, H, Nq), dtype=torch.float32, device="cuda")
+    out = pkg.fused(q, k, v, w.scale, mask=tm, lse=L)
+    pkg.check_status(0)
+    Mb = np.broadcast_to(M, (B, H, Nq, Nk))
+    ref, ref_lse = oracle.attn_batched(inp.qf, kf, vf, w.scale, mask=Mb)
+    got, lse = out.float().cpu().numpy(), L.cpu().numpy()
+    nan_rows = np.isnan(ref).all(axis=-1)
+    assert nan_rows[..., 256:512].all()       # the two Q tiles above
+    assert (np.isnan(got) == np.isnan(ref)).all()
+    assert (np.isnan(lse) == np.isnan(ref_lse)).all()
+    assert _rel(got[~nan_rows], ref[~nan_rows]) <= 2e-2
+    assert np.abs(lse[~nan_rows] - ref_lse[~nan_rows]).max() <= 1e-3
+
+
 def test_dense_causal_mask_equals_causal_variant(pkg, wl):
     """A causal pattern given as an explicit i1 mask and run on the dense-mask
     path (every KV tile visited) gives the same bits as the causal
