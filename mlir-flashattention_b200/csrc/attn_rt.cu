@@ -529,7 +529,14 @@ int ensure(void** p, size_t* have, size_t need) {
 // device side dense ([rows][D]).
 cudaError_t copy_slice(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
                        size_t rows, cudaMemcpyKind kind, cudaStream_t s) {
+  // Dense rows: one linear copy (a 2D copy of 256-byte rows runs slower).
+  if (dpitch == width && spitch == width) return cudaMemcpyAsync(dst, src, width * rows, kind, s);
   return cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, kind, s);
+}
+
+// True if a [B, H, N, D] operand with element strides st is densely packed.
+bool packed4(const int64_t st[3], int64_t H, int64_t N, int64_t D) {
+  return st[2] == D && st[1] == N * D && st[0] == H * N * D;
 }
 
 // Run a call whose operands live in host memory: chunks of (batch, kv-head)
@@ -567,7 +574,21 @@ int run_staged(const AttnDesc& hd, int device) {
     const int64_t g0 = c * per_chunk;
     const int64_t gn = std::min<int64_t>(per_chunk, ngroups - g0);
     if (c >= kStageBufs) CUDA_TRY(cudaStreamWaitEvent(st.s_h2d, sb.d2h_done, 0));
-    for (int64_t g = 0; g < gn; ++g) {
+    // Packed operands: a chunk of consecutive (batch, kv-head) groups is one
+    // contiguous range of Q, K, V (and O, LSE): one linear copy each.
+    const bool packed = packed4(hd.q_stride, hd.Hq, hd.Nq, hd.D) &&
+                        packed4(hd.k_stride, hd.Hkv, hd.Nk, hd.D) &&
+                        packed4(hd.v_stride, hd.Hkv, hd.Nk, hd.D) &&
+                        packed4(hd.o_stride, hd.Hq, hd.Nq, hd.D);
+    if (packed) {
+      CUDA_TRY(cudaMemcpyAsync(sb.k, static_cast<const char*>(hd.k) + g0 * kv_slice,
+                               gn * kv_slice, cudaMemcpyHostToDevice, st.s_h2d));
+      CUDA_TRY(cudaMemcpyAsync(sb.v, static_cast<const char*>(hd.v) + g0 * kv_slice,
+                               gn * kv_slice, cudaMemcpyHostToDevice, st.s_h2d));
+      CUDA_TRY(cudaMemcpyAsync(sb.q, static_cast<const char*>(hd.q) + g0 * group * q_slice,
+                               gn * group * q_slice, cudaMemcpyHostToDevice, st.s_h2d));
+    }
+    for (int64_t g = 0; g < gn && !packed; ++g) {
       const int64_t b = (g0 + g) / hd.Hkv, hk = (g0 + g) % hd.Hkv;
       const char* ks = static_cast<const char*>(hd.k) + (b * hd.k_stride[0] + hk * hd.k_stride[1]) * eb;
       const char* vs = static_cast<const char*>(hd.v) + (b * hd.v_stride[0] + hk * hd.v_stride[1]) * eb;
@@ -608,7 +629,15 @@ int run_staged(const AttnDesc& hd, int device) {
     if (rc != ATTN_OK) return rc;
     CUDA_TRY(cudaEventRecord(sb.comp_done, st.s_compute));
     CUDA_TRY(cudaStreamWaitEvent(st.s_d2h, sb.comp_done, 0));
-    for (int64_t g = 0; g < gn; ++g) {
+    if (packed) {
+      CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(hd.o) + g0 * group * o_slice, sb.o,
+                               gn * group * o_slice, cudaMemcpyDeviceToHost, st.s_d2h));
+      if (hd.lse)
+        CUDA_TRY(cudaMemcpyAsync(hd.lse + g0 * group * hd.Nq, sb.lse,
+                                 sizeof(float) * gn * group * hd.Nq, cudaMemcpyDeviceToHost,
+                                 st.s_d2h));
+    }
+    for (int64_t g = 0; g < gn && !packed; ++g) {
       const int64_t b = (g0 + g) / hd.Hkv, hk = (g0 + g) % hd.Hkv;
       for (int64_t i = 0; i < group; ++i) {
         const int64_t h = hk * group + i;
