@@ -270,10 +270,12 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime  # noqa: PLC0415
-        # Keep rank 0's stdout to the one JSON line (NCCL's version banner
-        # goes to stdout when NCCL_DEBUG=VERSION).
+        # Keep rank 0's stdout to the one JSON line: NCCL writes its log,
+        # including the version banner it prints at the WARN and VERSION
+        # levels, to stdout unless NCCL_DEBUG_FILE names another file.
         if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
             os.environ["NCCL_DEBUG"] = "WARN"
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
