@@ -190,7 +190,8 @@ def classify_mask(mask) -> int:
 
 
 def fused(Q, K, V, scale, mask=None, output=None, *, causal=False, lse=None,
-          q_descale=1.0, k_descale=1.0, v_descale=1.0, stream=None, sync_check=False):
+          q_descale=1.0, k_descale=1.0, v_descale=1.0, stream=None, sync_check=False,
+          classify=True):
     """Run ``attention.fused ins(Q, K, V) scale(scale) [mask(mask)] outs(output)``.
 
     Q: [Nq, D] or [B, Hq, Nq, D]; K, V: [Nk, D] or [B, Hkv, Nk, D] (Hq a
@@ -206,6 +207,8 @@ def fused(Q, K, V, scale, mask=None, output=None, *, causal=False, lse=None,
     e4m3 dequantisation factors are per tensor (Python floats) or per block
     (f32 CUDA tensors): ``q_descale`` [B, Hq, ceil(Nq/128)] (one per 128-row
     block of Q), ``k_descale`` [B, Hkv, ceil(Nk/128)], ``v_descale`` [B, Hkv].
+    ``classify=False`` runs a given mask on the dense-mask kernel as it is
+    (no check for the causal or empty pattern).
     """
     import torch  # noqa: PLC0415
     q4 = _as4(Q, "Q", "seq_q", "head_dim")
@@ -238,7 +241,7 @@ def fused(Q, K, V, scale, mask=None, output=None, *, causal=False, lse=None,
     if mask is not None:
         if mask.shape[-2:] != (Nq, k4.shape[2]):
             raise VerifyError("mask must be [seq_q, seq_k]")
-        kind = classify_mask(mask)
+        kind = classify_mask(mask) if classify else MASK_DENSE
         if causal and kind not in (MASK_NONE, MASK_CAUSAL):
             mask_kind = MASK_DENSE
         elif not causal:

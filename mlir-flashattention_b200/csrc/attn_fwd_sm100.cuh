@@ -839,53 +839,57 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Classes of the 128 x 128 blocks of a dense mask, for the dense mode's KV
-// tile skipping.  One CTA per (mask slice, Q tile), thread r owning mask row
-// 128·qt + r; per KV tile the CTA ORs "some key visible" and "some key masked"
-// over its rows (rows >= Nq ignored) and writes kTileEmpty, kTilePartial
-// (also every tile reaching past Nk) or kTileFull.  Reads each distinct mask
-// slice once: HBM-bound, Nq·Nk bytes per slice.
-__global__ void __launch_bounds__(128)
+// tile skipping.  One warp per block (8 per CTA): on the vector path lanes
+// 8r..8r+7 read row r's 128 bytes as 16-byte words, four rows per load, so
+// every load instruction takes four whole 128-byte lines; the warp ORs "some
+// key visible" and "some key masked" over the block's rows (rows >= Nq
+// ignored) and writes kTileEmpty, kTilePartial (also every block reaching past
+// Nk) or kTileFull.  Reads each distinct mask slice once: HBM-bound.
+constexpr int kClassifyWarps = 8;
+
+__global__ void __launch_bounds__(kClassifyWarps * 32)
     classify_mask_tiles(const uint8_t* __restrict__ mask, int64_t m_sb, int64_t m_sh,
                         int64_t m_sn, int Hm, int nqt, int Nq, int Nk, int nkt, int vec,
-                        uint8_t* __restrict__ cls) {
-  const int qt = static_cast<int>(blockIdx.x % static_cast<unsigned>(nqt));
-  const int slice = static_cast<int>(blockIdx.x / static_cast<unsigned>(nqt));
+                        uint8_t* __restrict__ cls, int64_t nblocks) {
+  const int lane = static_cast<int>(threadIdx.x) & 31;
+  const int64_t blk = static_cast<int64_t>(blockIdx.x) * kClassifyWarps + (threadIdx.x >> 5);
+  if (blk >= nblocks) return;  // whole warps only
+  const int kt = static_cast<int>(blk % nkt);
+  const int64_t sq = blk / nkt;  // slice * nqt + qt
+  const int qt = static_cast<int>(sq % nqt);
+  const int slice = static_cast<int>(sq / nqt);
   const int bm = slice / Hm, hm = slice - (slice / Hm) * Hm;
-  const int row = qt * 128 + static_cast<int>(threadIdx.x);
-  const bool live = row < Nq;
-  const uint8_t* mrow = mask + bm * m_sb + hm * m_sh + static_cast<int64_t>(min(row, Nq - 1)) * m_sn;
-  uint8_t* out = cls + static_cast<int64_t>(blockIdx.x) * nkt;
-  for (int kt = 0; kt < nkt; ++kt) {
-    const int kbase = kt * 128;
-    bool vis = false, msk = false;
-    if (live) {
-      if (vec && kbase + 128 <= Nk) {
-        const uint4* src = reinterpret_cast<const uint4*>(mrow + kbase);
+  const uint8_t* base = mask + bm * m_sb + hm * m_sh;
+  const int row0 = qt * 128, kbase = kt * 128;
+  const int rows = min(128, Nq - row0);
+  bool vis = false, msk = false;
+  if (vec && kbase + 128 <= Nk) {
+    const int sub = lane >> 3, word = lane & 7;  // row within a group of 4, 16-byte word
+    for (int r = sub; r < rows; r += 4) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(base + static_cast<int64_t>(row0 + r) * m_sn +
+                                                           kbase) + word);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const uint4 v = __ldg(src + q);
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            msk |= w[e] != 0u;
-            vis |= ((w[e] - 0x01010101u) & ~w[e] & 0x80808080u) != 0u;  // some byte is 0
-          }
-        }
-      } else {
-        const int lim = min(128, Nk - kbase);
-        for (int c = 0; c < lim; ++c) {
-          const bool m = mrow[kbase + c] != 0;
-          msk |= m;
-          vis |= !m;
-        }
+      for (int e = 0; e < 4; ++e) {
+        msk |= w[e] != 0u;
+        vis |= ((w[e] - 0x01010101u) & ~w[e] & 0x80808080u) != 0u;  // some byte is 0
       }
     }
-    const int any_vis = __syncthreads_or(vis);
-    const int any_msk = __syncthreads_or(msk);
-    if (threadIdx.x == 0)
-      out[kt] = !any_vis ? kTileEmpty
-                         : ((any_msk || kbase + 128 > Nk) ? kTilePartial : kTileFull);
+  } else {
+    const int lim = min(128, Nk - kbase);
+    for (int r = 0; r < rows; ++r) {
+      const uint8_t* mrow = base + static_cast<int64_t>(row0 + r) * m_sn + kbase;
+      for (int c = lane; c < lim; c += 32) {
+        const bool m = mrow[c] != 0;
+        msk |= m;
+        vis |= !m;
+      }
+    }
   }
+  const bool any_vis = __any_sync(0xffffffffu, vis);
+  const bool any_msk = __any_sync(0xffffffffu, msk);
+  if (lane == 0)
+    cls[blk] = !any_vis ? kTileEmpty : ((any_msk || kbase + 128 > Nk) ? kTilePartial : kTileFull);
 }
 
 }  // namespace attn_sm100

@@ -256,15 +256,17 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
     const int64_t nqt = (d.Nq + 127) / 128, nkt = (d.Nk + 127) / 128;
     const int64_t Bm = (d.B == 1 || d.mask_stride[0] == 0) ? 1 : d.B;
     const int64_t Hm = (d.Hq == 1 || d.mask_stride[1] == 0) ? 1 : d.Hq;
-    const int64_t blocks = Bm * Hm * nqt;
-    if (blocks >= (1ll << 31)) return fail(ATTN_ERR_SHAPE, "dense mask too large to classify");
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&cls),
-                                    static_cast<size_t>(blocks * nkt), stream);
+    const int64_t blocks = Bm * Hm * nqt * nkt;  // one warp each
+    const int64_t ctas = (blocks + attn_sm100::kClassifyWarps - 1) / attn_sm100::kClassifyWarps;
+    if (ctas >= (1ll << 31)) return fail(ATTN_ERR_SHAPE, "dense mask too large to classify");
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&cls), static_cast<size_t>(blocks),
+                                    stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync (mask tile classes)");
-    attn_sm100::classify_mask_tiles<<<static_cast<unsigned>(blocks), 128, 0, stream>>>(
+    attn_sm100::classify_mask_tiles<<<static_cast<unsigned>(ctas), attn_sm100::kClassifyWarps * 32,
+                                      0, stream>>>(
         d.mask, Bm == 1 ? 0 : d.mask_stride[0], Hm == 1 ? 0 : d.mask_stride[1], d.mask_stride[2],
         static_cast<int>(Hm), static_cast<int>(nqt), static_cast<int>(d.Nq),
-        static_cast<int>(d.Nk), static_cast<int>(nkt), p.mask_vec, cls);
+        static_cast<int>(d.Nk), static_cast<int>(nkt), p.mask_vec, cls, blocks);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
       cudaFreeAsync(cls, stream);

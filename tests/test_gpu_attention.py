@@ -389,3 +389,90 @@ def test_f16_parity(pkg, oracle, D, causal):
                                        causal=causal)
     assert _rel(out.float().cpu().numpy(), ref) <= 1e-2
     assert np.abs(L.cpu().numpy() - ref_lse).max() <= 1e-3
+
+
+def test_host_memref_pipeline_strided_equals_device(pkg, wl):
+    """Host memrefs whose heads are not packed ([B, N, H, D] storage viewed as
+    [B, H, N, D]) take the per-slice staging copies; same bits as the device
+    call on the same views."""
+    w = wl.Workload("t", "bf16", 2, 4, 4, 384, 64, False, seed=19)
+    inp = wl.make_inputs(w)
+    q, k, v = (t.transpose(1, 2).contiguous().transpose(1, 2) for t in wl.to_device(inp, w))
+    assert not q.is_contiguous()
+    L_dev = torch.empty((2, 4, 384), dtype=torch.float32, device="cuda")
+    ref = pkg.fused(q, k, v, w.scale, lse=L_dev)
+    pkg.check_status(0)
+    hq, hk, hv = (t.cpu().transpose(1, 2).contiguous().pin_memory().transpose(1, 2)
+                  for t in (q, k, v))
+    ho = torch.empty((2, 384, 4, 64), dtype=torch.bfloat16).pin_memory().transpose(1, 2)
+    hl = torch.empty((2, 4, 384, 1), dtype=torch.float32).pin_memory()
+    rc = pkg.lib()._mlir_ciface_attn_fused_bf16_nomask_4d(
+        pkg.memref(hq), pkg.memref(hk), pkg.memref(hv), w.scale, pkg.memref(ho), pkg.memref(hl))
+    assert rc == 0, pkg.last_error()
+    assert torch.equal(ho, ref.cpu())
+    assert torch.equal(hl[..., 0], L_dev.cpu())
+
+
+def _block_mask(rng, shape, nq, nk):
+    """Random 128 x 128 block structure (visible / masked / mixed blocks)."""
+    nqt, nkt = -(-nq // 128), -(-nk // 128)
+    kind = rng.choice(3, size=shape + (nqt, nkt), p=[0.4, 0.3, 0.3])
+    kind[..., 0] = 2  # first KV tile mixed: no NaN rows
+    M = np.zeros(shape + (nqt * 128, nkt * 128), bool)
+    for idx in np.ndindex(*kind.shape):
+        r0, c0 = idx[-2] * 128, idx[-1] * 128
+        blk = M[idx[:-2]][r0:r0 + 128, c0:c0 + 128]
+        if kind[idx] == 1:
+            blk[:] = True
+        elif kind[idx] == 2:
+            blk[:] = rng.random((128, 128)) < 0.4
+            blk[:, 0] = False
+    return np.ascontiguousarray(M[..., :nq, :nk])
+
+
+@pytest.mark.parametrize("dtype", ["f16", "e4m3"])
+def test_dense_block_mask_gqa_other_types(pkg, wl, oracle, dtype):
+    """Dense block masks with grouped-query heads on f16 inputs and on e4m3
+    inputs with per-block factors (mask per query head, blocks skipped)."""
+    rng = np.random.default_rng(5 if dtype == "f16" else 6)
+    B, Hq, Hkv, Nq, Nk, D = 2, 4, 2, 520, 700, 128
+    M = _block_mask(rng, (B, Hq), Nq, Nk)
+    q = rng.standard_normal((B, Hq, Nq, D)).astype(np.float32)
+    k = rng.standard_normal((B, Hkv, Nk, D)).astype(np.float32)
+    v = rng.standard_normal((B, Hkv, Nk, D)).astype(np.float32)
+    if dtype == "f16":
+        qf, kf, vf = (a.astype(np.float16).astype(np.float32) for a in (q, k, v))
+        dev = [torch.from_numpy(a.astype(np.float16)).cuda() for a in (q, k, v)]
+        kw, tol = {}, 1e-2
+    else:
+        (q8, qd, qf), (k8, kd, kf), (v8, vd, vf) = (
+            wl.quant_e4m3_blocks(q), wl.quant_e4m3_blocks(k), wl.quant_e4m3_heads(v))
+        dev = [torch.from_numpy(a).cuda() for a in (q8, k8, v8)]
+        kw = dict(q_descale=torch.from_numpy(qd).cuda(), k_descale=torch.from_numpy(kd).cuda(),
+                  v_descale=torch.from_numpy(vd).cuda())
+        tol = 6e-2
+    L = torch.empty((B, Hq, Nq), dtype=torch.float32, device="cuda")
+    out = pkg.fused(*dev, D ** -0.5, mask=torch.from_numpy(M).cuda(), lse=L, **kw)
+    pkg.check_status(0)
+    ref, ref_lse = oracle.attn_batched(qf, kf, vf, D ** -0.5, mask=M)
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all() and np.isfinite(ref).all()
+    for b in range(B):
+        for h in range(Hq):
+            assert _rel(got[b, h], ref[b, h]) <= tol, (b, h)
+    assert np.abs(L.cpu().numpy() - ref_lse).max() <= 1e-2
+
+
+def test_dense_block_mask_f32_output(pkg, wl, oracle):
+    """bf16 inputs, f32 output, dense block mask broadcast over heads."""
+    rng = np.random.default_rng(8)
+    w = wl.Workload("t", "bf16", 1, 3, 3, 900, 128, False, seed=21)
+    inp = wl.make_inputs(w)
+    M = _block_mask(rng, (), 900, 900)
+    q, k, v = wl.to_device(inp, w)
+    out = torch.empty((1, 3, 900, 128), dtype=torch.float32, device="cuda")
+    pkg.fused(q, k, v, w.scale, mask=torch.from_numpy(M).cuda(), output=out)
+    pkg.check_status(0)
+    ref, _ = oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale,
+                                 mask=np.broadcast_to(M, (1, 3, 900, 900)))
+    assert _rel(out.cpu().numpy(), ref) <= 2e-2
