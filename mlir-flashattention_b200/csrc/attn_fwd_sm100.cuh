@@ -79,6 +79,9 @@ struct FwdParams {
   const uint8_t* tile_cls;
   int64_t cls_sb, cls_sh;
   int nkt;
+  // Dense mode: work items (slice-major index) ordered by decreasing number
+  // of KV tiles visited (order_dense_items), for the persistent schedule.
+  const int* order;
 };
 
 // Classes of a 128 x 128 block of a dense mask (rows < Nq, keys < Nk).
@@ -367,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int r = 0; ok; ++r) {
           const int w = item_index<CAUSAL>(r, cta, G, W);
           if (w < 0) break;
-          const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
+          const Item itm = decode_item<CAUSAL>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs);
           const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq, hk = h / p.group;
           const PairSched<MODE> sc = make_sched<MODE>(itm, p);
           const int kt_end = sc.end();
@@ -460,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int r = 0; ok; ++r) {
         const int w = item_index<CAUSAL>(r, cta, G, W);
         if (w < 0) break;
-        const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
+        const Item itm = decode_item<CAUSAL>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs);
         const PairSched<MODE> sc = make_sched<MODE>(itm, p);
         const int kt_end = sc.end();
         const int kt0 = sc.next(-1);
@@ -588,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int rr = 0; ok; ++rr) {
       const int w = item_index<CAUSAL>(rr, cta, G, W);
       if (w < 0) break;
-      const Item itm = decode_item<CAUSAL>(w, p.num_bh, p.num_pairs);
+      const Item itm = decode_item<CAUSAL>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs);
       const PairSched<MODE> sc = make_sched<MODE>(itm, p);
       const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq;
       const int qs = itm.pair * 256 + 128 * t;
@@ -850,7 +853,8 @@ constexpr int kClassifyWarps = 8;
 __global__ void __launch_bounds__(kClassifyWarps * 32)
     classify_mask_tiles(const uint8_t* __restrict__ mask, int64_t m_sb, int64_t m_sh,
                         int64_t m_sn, int Hm, int nqt, int Nq, int Nk, int nkt, int vec,
-                        uint8_t* __restrict__ cls, int64_t nblocks) {
+                        uint8_t* __restrict__ cls, int* __restrict__ row_count,
+                        int64_t nblocks) {
   const int lane = static_cast<int>(threadIdx.x) & 31;
   const int64_t blk = static_cast<int64_t>(blockIdx.x) * kClassifyWarps + (threadIdx.x >> 5);
   if (blk >= nblocks) return;  // whole warps only
@@ -888,8 +892,62 @@ __global__ void __launch_bounds__(kClassifyWarps * 32)
   }
   const bool any_vis = __any_sync(0xffffffffu, vis);
   const bool any_msk = __any_sync(0xffffffffu, msk);
-  if (lane == 0)
+  if (lane == 0) {
     cls[blk] = !any_vis ? kTileEmpty : ((any_msk || kbase + 128 > Nk) ? kTilePartial : kTileFull);
+    if (any_vis) atomicAdd(row_count + sq, 1);  // non-empty blocks per (slice, Q tile)
+  }
+}
+
+// Work list order for the dense mode: pairs sorted by decreasing weight
+// (the KV tiles their two Q tiles visit: the non-empty blocks counted per
+// (slice, Q tile) by classify_mask_tiles, 0 for a tile whose first block is
+// empty), so the persistent CTAs' snake takes the heaviest pairs first, as
+// the causal mode's fixed order does.  One CTA: weights, a counting sort over
+// at most kOrderBuckets weights (more: the slice-major identity order),
+// scatter.
+// Items of equal weight may land in any order; each item is computed the
+// same way wherever it lands.
+constexpr int kOrderBuckets = 4096;
+
+__global__ void __launch_bounds__(1024)
+    order_dense_items(const uint8_t* __restrict__ cls, const int* __restrict__ row_count,
+                      int64_t cls_sb, int64_t cls_sh, int Hq, int num_bh, int num_pairs, int nqt,
+                      int nkt, uint16_t* __restrict__ weight, int* __restrict__ order) {
+  __shared__ int start[kOrderBuckets];
+  const int items = num_bh * num_pairs;
+  const int nb = 2 * nkt + 1;
+  if (nb > kOrderBuckets) {
+    for (int i = threadIdx.x; i < items; i += blockDim.x) order[i] = i;
+    return;
+  }
+  for (int k = threadIdx.x; k < nb; k += blockDim.x) start[k] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    const int bh = i / num_pairs, pair = i - (i / num_pairs) * num_pairs;
+    const int b = bh / Hq, h = bh - (bh / Hq) * Hq;
+    int wgt = 0;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int qt = 2 * pair + t;
+      if (qt >= nqt) continue;
+      const int64_t r = (b * cls_sb + h * cls_sh) / nkt + qt;  // (slice, Q tile)
+      if (cls[r * nkt] == kTileEmpty) continue;  // NaN tile: no KV tile visited
+      wgt += row_count[r];
+    }
+    weight[i] = static_cast<uint16_t>(wgt);
+    atomicAdd(&start[wgt], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // heaviest first: exclusive sum over decreasing weights
+    int acc = 0;
+    for (int k = nb - 1; k >= 0; --k) {
+      const int c = start[k];
+      start[k] = acc;
+      acc += c;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < items; i += blockDim.x) order[atomicAdd(&start[weight[i]], 1)] = i;
 }
 
 }  // namespace attn_sm100

@@ -258,15 +258,31 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
     const int64_t Hm = (d.Hq == 1 || d.mask_stride[1] == 0) ? 1 : d.Hq;
     const int64_t blocks = Bm * Hm * nqt * nkt;  // one warp each
     const int64_t ctas = (blocks + attn_sm100::kClassifyWarps - 1) / attn_sm100::kClassifyWarps;
+    const int64_t items = static_cast<int64_t>(p.num_bh) * p.num_pairs;
     if (ctas >= (1ll << 31)) return fail(ATTN_ERR_SHAPE, "dense mask too large to classify");
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&cls), static_cast<size_t>(blocks),
+    // One scratch block: classes, non-empty blocks per (slice, Q tile) (i32),
+    // item weights (u16), the work order (i32).
+    auto r256 = [](size_t n) { return (n + 255) / 256 * 256; };
+    const size_t cls_bytes = r256(static_cast<size_t>(blocks));
+    const size_t cnt_bytes = r256(static_cast<size_t>(Bm * Hm * nqt) * 4);
+    const size_t w_bytes = r256(static_cast<size_t>(items) * 2);
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&cls),
+                                    cls_bytes + cnt_bytes + w_bytes + static_cast<size_t>(items) * 4,
                                     stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync (mask tile classes)");
+    int* row_count = reinterpret_cast<int*>(cls + cls_bytes);
+    uint16_t* weights = reinterpret_cast<uint16_t*>(cls + cls_bytes + cnt_bytes);
+    int* order = reinterpret_cast<int*>(cls + cls_bytes + cnt_bytes + w_bytes);
+    e = cudaMemsetAsync(row_count, 0, cnt_bytes, stream);
+    if (e != cudaSuccess) {
+      cudaFreeAsync(cls, stream);
+      return cuda_fail(e, "cudaMemsetAsync (mask block counts)");
+    }
     attn_sm100::classify_mask_tiles<<<static_cast<unsigned>(ctas), attn_sm100::kClassifyWarps * 32,
                                       0, stream>>>(
         d.mask, Bm == 1 ? 0 : d.mask_stride[0], Hm == 1 ? 0 : d.mask_stride[1], d.mask_stride[2],
         static_cast<int>(Hm), static_cast<int>(nqt), static_cast<int>(d.Nq),
-        static_cast<int>(d.Nk), static_cast<int>(nkt), p.mask_vec, cls, blocks);
+        static_cast<int>(d.Nk), static_cast<int>(nkt), p.mask_vec, cls, row_count, blocks);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
       cudaFreeAsync(cls, stream);
@@ -277,6 +293,16 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
     p.cls_sb = Bm == 1 ? 0 : Hm * nqt * nkt;
     p.cls_sh = Hm == 1 ? 0 : nqt * nkt;
     p.nkt = static_cast<int>(nkt);
+    attn_sm100::order_dense_items<<<1, 1024, 0, stream>>>(
+        cls, row_count, p.cls_sb, p.cls_sh, p.Hq, p.num_bh, p.num_pairs, static_cast<int>(nqt),
+        p.nkt, weights, order);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      cudaFreeAsync(cls, stream);
+      return cuda_fail(e, "order_dense_items launch");
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    p.order = order;
   }
   // Persistent launch: one CTA per SM (TMEM and shared memory allow one),
   // each walking its share of the (slice, Q-tile pair) work list.
