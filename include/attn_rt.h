@@ -106,7 +106,10 @@ typedef struct AttnDesc {
 } AttnDesc;
 
 /* Asynchronous launch on `stream` (a cudaStream_t; NULL = legacy default).
- * Replaces the loop nest TilingPass.cpp:188-386 emits for one attention.fused. */
+ * Replaces the loop nest TilingPass.cpp:188-386 emits for one attention.fused.
+ * Empty extents behave as that loop nest does: B, Hq or Nq = 0 computes
+ * nothing (ATTN_OK); Nk = 0 runs no KV step, so every row of O is 0/0 = NaN
+ * and the LSE is -inf. */
 ATTN_API int attn_fwd(const AttnDesc* desc, void* stream);
 
 /* Select and initialise `device` (idempotent): checks for sm_100, creates the

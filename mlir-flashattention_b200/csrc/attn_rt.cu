@@ -14,6 +14,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <limits>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -376,6 +377,67 @@ __global__ void probe_timeout_kernel(uint64_t limit_ns, int32_t* status) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Empty extents, handled as the reference's loop nest (TilingPass.cpp:188,208)
+// handles them: no query row (B, Hq or Nq = 0) computes nothing; no key
+// (Nk = 0) runs no KV step, leaving O_acc = 0 and l = 0, so every output row
+// is 0/0 = NaN and the LSE m + ln l is -inf.  Sets the two flags; the full
+// validation (validate) applies only to calls with rows and keys.
+int check_empty(const AttnDesc& d, bool* no_rows, bool* no_keys) {
+  *no_rows = *no_keys = false;
+  if (d.B < 0 || d.Hq < 0 || d.Hkv < 0 || d.Nq < 0 || d.Nk < 0 || d.D < 0)
+    return fail(ATTN_ERR_SHAPE, "extents must not be negative");
+  const bool rows = d.B == 0 || d.Hq == 0 || d.Nq == 0;
+  if (!rows && d.Nk != 0) return ATTN_OK;
+  if (d.flags != 0) return fail(ATTN_ERR_INVALID, "flags must be 0");
+  if (d.dtype != ATTN_F32 && d.dtype != ATTN_BF16 && d.dtype != ATTN_F16 && d.dtype != ATTN_E4M3)
+    return fail(ATTN_ERR_DTYPE, "unknown dtype %d", d.dtype);
+  if (d.out_dtype != ATTN_F32 && d.out_dtype != ATTN_BF16 && d.out_dtype != ATTN_F16)
+    return fail(ATTN_ERR_DTYPE, "unknown output dtype %d", d.out_dtype);
+  if (d.mask_kind < ATTN_MASK_NONE || d.mask_kind > ATTN_MASK_DENSE)
+    return fail(ATTN_ERR_INVALID, "unknown mask kind %d", d.mask_kind);
+  if (d.Hq > 0 && (d.Hkv <= 0 || d.Hq % d.Hkv != 0))
+    return fail(ATTN_ERR_SHAPE, "query heads (%lld) must be a multiple of key/value heads (%lld)",
+                (long long)d.Hq, (long long)d.Hkv);
+  *no_rows = rows;
+  *no_keys = !rows;
+  if (*no_keys && d.D > 0 && !d.o) return fail(ATTN_ERR_INVALID, "null output pointer");
+  return ATTN_OK;
+}
+
+// Output of a call without keys, in device memory: O rows NaN, LSE -inf.
+__global__ void fill_no_keys(void* o, int out_kind, int64_t sb, int64_t sh, int64_t sn, int64_t Hq,
+                             int64_t Nq, int64_t D, float* lse, int64_t rows) {
+  const int64_t total = rows * D;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / D, c = i - (i / D) * D;  // r = (b * Hq + h) * Nq + n
+    const int64_t n = r % Nq, bh = r / Nq, b = bh / Hq, h = bh % Hq;
+    const int64_t off = b * sb + h * sh + n * sn + c;
+    if (out_kind == 1)
+      static_cast<float*>(o)[off] = __int_as_float(0x7fc00000);
+    else
+      static_cast<uint16_t*>(o)[off] = out_kind == 2 ? 0x7e00 : 0x7fc0;
+    if (lse && c == 0) lse[r] = -INFINITY;
+  }
+}
+
+// The same in host memory (host memref operands).
+void fill_no_keys_host(const AttnDesc& d) {
+  for (int64_t b = 0; b < d.B; ++b)
+    for (int64_t h = 0; h < d.Hq; ++h)
+      for (int64_t n = 0; n < d.Nq; ++n) {
+        const int64_t off = b * d.o_stride[0] + h * d.o_stride[1] + n * d.o_stride[2];
+        for (int64_t c = 0; c < d.D; ++c) {
+          if (d.out_dtype == ATTN_F32) {
+            static_cast<float*>(d.o)[off + c] = std::numeric_limits<float>::quiet_NaN();
+          } else {
+            static_cast<uint16_t*>(d.o)[off + c] = d.out_dtype == ATTN_F16 ? 0x7e00 : 0x7fc0;
+          }
+        }
+        if (d.lse) d.lse[(b * d.Hq + h) * d.Nq + n] = -std::numeric_limits<float>::infinity();
+      }
+}
+
 int validate(const AttnDesc& d) {
   if (!d.q || !d.k || !d.v || !d.o) return fail(ATTN_ERR_INVALID, "null Q/K/V/output pointer");
   if (d.flags != 0) return fail(ATTN_ERR_INVALID, "flags must be 0");
@@ -726,7 +788,14 @@ int run_views(int dtype, int out_dtype, int mask_kind, const View& Q, const View
     d.mask_stride[1] = M->size[1] == 1 ? 0 : M->stride[1];
     d.mask_stride[2] = M->stride[2];
   }
-  const bool dev_q = is_device_ptr(d.q);
+  bool no_rows = false, no_keys = false;
+  if ((rc = check_empty(d, &no_rows, &no_keys)) != ATTN_OK) return rc;
+  if (no_rows) return ATTN_OK;
+  if (no_keys && !is_device_ptr(d.o)) {
+    fill_no_keys_host(d);
+    return ATTN_OK;
+  }
+  const bool dev_q = no_keys || is_device_ptr(d.q);
   if (dev_q) {
     if (!is_device_ptr(d.k) || !is_device_ptr(d.v) || !is_device_ptr(d.o) ||
         (d.lse && !is_device_ptr(d.lse)) || (d.mask && !is_device_ptr(d.mask)))
@@ -841,11 +910,27 @@ int attn_rt_check_status(int device, void* stream) {
 
 int attn_fwd(const AttnDesc* desc, void* stream) {
   if (!desc) return fail(ATTN_ERR_INVALID, "null descriptor");
-  int rc = validate(*desc);
+  bool no_rows = false, no_keys = false;
+  int rc = check_empty(*desc, &no_rows, &no_keys);
   if (rc != ATTN_OK) return rc;
+  if (no_rows) return ATTN_OK;
+  if (!no_keys && (rc = validate(*desc)) != ATTN_OK) return rc;
   int dev = 0;
   if ((rc = current_device(&dev)) != ATTN_OK) return rc;
   if ((rc = init_device(dev)) != ATTN_OK) return rc;
+  if (no_keys) {
+    const AttnDesc& d = *desc;
+    const int64_t rows = d.B * d.Hq * d.Nq;
+    if (rows * d.D == 0) return ATTN_OK;
+    const int out_kind = d.out_dtype == ATTN_F32 ? 1 : (d.out_dtype == ATTN_F16 ? 2 : 0);
+    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((rows * d.D + 255) / 256, 4096));
+    fill_no_keys<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        d.o, out_kind, d.o_stride[0], d.o_stride[1], d.o_stride[2], d.Hq, d.Nq, d.D, d.lse, rows);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "fill_no_keys launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return ATTN_OK;
+  }
   int32_t* status = desc->status ? desc->status : g_dev[dev].status;
   return dispatch(*desc, status, static_cast<cudaStream_t>(stream));
 }
@@ -980,7 +1065,15 @@ extern "C" int attn_fwd_host_noalloc(const AttnDesc* desc, void* stream_) {
     return fail(ATTN_ERR_UNSUPPORTED, "attn_fwd_host_noalloc supports no-mask and causal calls");
   if (hd.q_descale_blocks || hd.k_descale_blocks || hd.v_descale_heads)
     return fail(ATTN_ERR_UNSUPPORTED, "attn_fwd_host_noalloc takes per-tensor descales only");
-  int rc = validate(hd);
+  bool no_rows = false, no_keys = false;
+  int rc = check_empty(hd, &no_rows, &no_keys);
+  if (rc != ATTN_OK) return rc;
+  if (no_rows) return ATTN_OK;
+  if (no_keys) {
+    fill_no_keys_host(hd);
+    return ATTN_OK;
+  }
+  rc = validate(hd);
   if (rc != ATTN_OK) return rc;
   int dev = 0;
   if ((rc = current_device(&dev)) != ATTN_OK) return rc;

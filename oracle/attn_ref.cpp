@@ -186,7 +186,11 @@ extern "C" {
 int oracle_attn_fused_f32(const float* Q, const float* K, const float* V, float scale,
                           const uint8_t* mask, int causal, float* O, float* lse, int64_t Nq,
                           int64_t Nk, int64_t D, int64_t T) {
-  if (!Q || !K || !V || !O || Nq <= 0 || Nk <= 0 || D <= 0 || T <= 0) return -1;
+  // Empty extents run the same loop nest: no query row does nothing; no key
+  // leaves O_acc = 0 and l = 0, so O = 0/0 = NaN and LSE = -inf.
+  if (Nq < 0 || Nk < 0 || D <= 0 || T <= 0) return -1;
+  if (Nq == 0) return 0;
+  if (!Q || !O || (Nk > 0 && (!K || !V))) return -1;
   SliceArgs a{Q, K, V, O, lse, mask, D, D, D, D, Nk, Nq, Nk, D, scale, causal, T};
   for (int64_t i0 = 0; i0 < Nq; i0 += T) q_tile(a, i0);
   return 0;
@@ -202,9 +206,10 @@ int oracle_attn_batched(const float* Q, const float* K, const float* V, float* O
                         float scale, int causal, const uint8_t* mask, int64_t T, int nthreads,
                         const int64_t* slices, int64_t nslices, int64_t tile_offset,
                         int64_t tile_stride) {
-  if (!Q || !K || !V || !O || B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Nq <= 0 || Nk <= 0 ||
-      D <= 0 || T <= 0)
+  if (B < 0 || Hq < 0 || Hkv <= 0 || Hq % Hkv || Nq < 0 || Nk < 0 || D <= 0 || T <= 0)
     return -1;
+  if (B == 0 || Hq == 0 || Nq == 0) return 0;  // no query row: nothing to compute
+  if (!Q || !O || (Nk > 0 && (!K || !V))) return -1;
   if (tile_stride <= 0) tile_stride = 1;
   const int64_t group = Hq / Hkv;
   const int64_t ntiles = (Nq + T - 1) / T;

@@ -59,7 +59,7 @@ def _desc(pkg, **kw):
 
 @pytest.mark.parametrize("field,value,code", [
     ("Hkv", 3, -2),          # heads not a multiple
-    ("Nk", 0, -2),           # empty extent
+    ("Nk", -1, -2),          # negative extent
     ("D", 96, -8),           # bf16 head_dim not built
     ("dtype", 7, -4),
     ("mask_kind", 2, -1),    # dense without a mask pointer

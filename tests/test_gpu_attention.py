@@ -476,3 +476,34 @@ def test_dense_block_mask_f32_output(pkg, wl, oracle):
     ref, _ = oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale,
                                  mask=np.broadcast_to(M, (1, 3, 900, 900)))
     assert _rel(out.cpu().numpy(), ref) <= 2e-2
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_empty_extents_match_the_reference_loop(pkg, oracle, dtype):
+    """No key: every output row NaN and LSE -inf (the reference's loop never
+    runs a KV step, O = 0/0); no query row: a no-op.  Device tensors and host
+    memrefs."""
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    q = torch.randn((2, 3, 200, 64), device="cuda").to(tdt)
+    none = torch.empty((2, 3, 0, 64), device="cuda", dtype=tdt)
+    L = torch.zeros((2, 3, 200), dtype=torch.float32, device="cuda")
+    out = pkg.fused(q, none, none, 0.125, lse=L)
+    pkg.check_status(0)
+    ref, ref_lse = oracle.attn_batched(q.float().cpu().numpy(), none.float().cpu().numpy(),
+                                       none.float().cpu().numpy(), 0.125)
+    assert torch.isnan(out).all() and np.isnan(ref).all()
+    assert torch.isneginf(L).all() and np.isneginf(ref_lse).all()
+    # no query row: the output is left untouched
+    q0 = torch.empty((2, 3, 0, 64), device="cuda", dtype=tdt)
+    k = torch.randn((2, 3, 50, 64), device="cuda").to(tdt)
+    o0 = pkg.fused(q0, k, k, 0.125)
+    pkg.check_status(0)
+    assert o0.shape == (2, 3, 0, 64)
+    # host memrefs, rank-2 f32 form of the op
+    hq = torch.randn((40, 64))
+    hk = torch.empty((0, 64))
+    ho = torch.zeros((40, 64))
+    rc = pkg.lib()._mlir_ciface_attn_fused_f32_nomask(pkg.memref(hq), pkg.memref(hk),
+                                                      pkg.memref(hk), 0.125, pkg.memref(ho))
+    assert rc == 0, pkg.last_error()
+    assert torch.isnan(ho).all()

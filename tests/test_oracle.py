@@ -106,3 +106,18 @@ def test_quantisation_helpers(wl):
     assert r[0] == 1.0 and r[1] == 1.0 and r[2] == 1.015625
     codes, descale, deq = wl.quant_e4m3(np.array([0.5, -2.0, 4.0], np.float32))
     assert abs(descale - 4.0 / 448) < 1e-9 and abs(deq[2] - 4.0) < 1e-6
+
+
+def test_empty_extents_follow_the_loop_nest(oracle):
+    """No key: the KV loop never runs, O_acc = 0 and l = 0, so O = 0/0 = NaN and
+    LSE = -inf; no query row: nothing is computed."""
+    rng = np.random.default_rng(3)
+    q = rng.standard_normal((1, 2, 5, 64)).astype(np.float32)
+    none = np.zeros((1, 2, 0, 64), np.float32)
+    o, lse = oracle.attn_batched(q, none, none, 0.125)
+    assert np.isnan(o).all() and np.isneginf(lse).all()
+    o2, l2 = oracle.attn_fused_f32(q[0, 0], none[0, 0], none[0, 0], 0.125)
+    assert np.isnan(o2).all() and np.isneginf(l2).all()
+    k = rng.standard_normal((1, 2, 7, 64)).astype(np.float32)
+    o3, l3 = oracle.attn_batched(none, k, k, 0.125)
+    assert o3.shape == (1, 2, 0, 64) and l3.shape == (1, 2, 0)
