@@ -507,3 +507,42 @@ def test_empty_extents_match_the_reference_loop(pkg, oracle, dtype):
                                                       pkg.memref(hk), 0.125, pkg.memref(ho))
     assert rc == 0, pkg.last_error()
     assert torch.isnan(ho).all()
+
+
+def test_long_key_sequence_single_query_row(pkg, oracle):
+    """One query row against 262144 keys (2048 KV tiles in one online-softmax
+    chain, Nq far below a tile), bf16 with LSE."""
+    g = torch.Generator(device="cuda").manual_seed(31)
+    Nk, D = 262144, 128
+    q = torch.randn((1, 1, 1, D), generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn((1, 1, Nk, D), generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn((1, 1, Nk, D), generator=g, device="cuda").to(torch.bfloat16)
+    L = torch.empty((1, 1, 1), dtype=torch.float32, device="cuda")
+    out = pkg.fused(q, k, v, D ** -0.5, lse=L)
+    pkg.check_status(0)
+    ref, ref_lse = oracle.attn_batched(*(t.float().cpu().numpy() for t in (q, k, v)), D ** -0.5)
+    assert _rel(out.float().cpu().numpy(), ref) <= 2e-2
+    assert abs(float(L.item()) - float(ref_lse.ravel()[0])) <= 1e-3
+
+
+def test_long_causal_sequence_sampled_tiles(pkg, oracle):
+    """N = 65536 causal, one head: the first, a middle and the last Q tile
+    against the oracle (256 KV tiles on the longest rows)."""
+    g = torch.Generator(device="cuda").manual_seed(32)
+    N, D = 65536, 128
+    q, k, v = (torch.randn((1, 1, N, D), generator=g, device="cuda").to(torch.bfloat16)
+               for _ in range(3))
+    L = torch.empty((1, 1, N), dtype=torch.float32, device="cuda")
+    out = pkg.fused(q, k, v, D ** -0.5, causal=True, lse=L)
+    pkg.check_status(0)
+    got, lse = out.float().cpu().numpy(), L.cpu().numpy()
+    assert np.isfinite(got).all()
+    qf, kf, vf = (t.float().cpu().numpy() for t in (q, k, v))
+    ref = np.zeros_like(qf)
+    ref_lse = np.zeros((1, 1, N), np.float32)
+    oracle.attn_batched(qf, kf, vf, D ** -0.5, causal=True, tile_offset=0, tile_stride=255,
+                        out=ref, lse_out=ref_lse)
+    for t in (0, 255, 510):
+        rows = slice(t * 128, t * 128 + 128)
+        assert _rel(got[0, 0, rows], ref[0, 0, rows]) <= 2e-2, t
+        assert np.abs(lse[0, 0, rows] - ref_lse[0, 0, rows]).max() <= 1e-3, t
