@@ -15,7 +15,8 @@
 //   warp 9      MMA issuer (converged warp, one elected lane issues):
 //               S_t = Q_t·K_jᵀ into TMEM (SS form), O_t += P_t·V_j with P_t
 //               read from TMEM (TS form); order per KV step
-//               P·V_0(j), S_0(j+1), P·V_1(j), S_1(j+1).
+//               P·V_0(j), S_0(j'), P·V_1(j), S_1(j') where j' is the next
+//               KV tile of the pair's list (PairSched).
 //   warps 0-3   softmax for Q tile 0, warps 4-7 for Q tile 1: one thread per
 //               query row reads its S row from TMEM, applies the mask, updates
 //               (m, l) in registers, writes P (bf16 / f16 / e4m3) back into the
@@ -37,7 +38,9 @@
 // diagonal are never loaded or multiplied (the FULL / MASKED / BOUNDARY tile
 // split of the reference design, Design.md:412-419) and only diagonal and
 // ragged-edge tiles apply a per-element mask; dense: the op's i1 mask operand
-// (TilingPass.cpp:254-277) read per row and KV tile.
+// (TilingPass.cpp:254-277), whose 128 x 128 blocks classify_mask_tiles
+// classifies first: empty blocks are skipped like the causal ones, full
+// blocks need no mask bytes, partial blocks are read per row and KV tile.
 //
 // Hang safety: every mbarrier wait is bounded (wall-clock limit); on expiry
 // the CTA records ATTN_ERR_TIMEOUT in the status word, all roles leave their
