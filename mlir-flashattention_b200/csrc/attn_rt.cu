@@ -70,6 +70,9 @@ struct DevState {
   int32_t* status = nullptr;
   cudaStream_t s_compute = nullptr, s_h2d = nullptr, s_d2h = nullptr;
   Staging stage[kStageBufs];
+  std::mutex whole_mu;    // guards `whole` (held across one staged call)
+  void* whole = nullptr;  // whole-operand staging of host f32 / dense-mask calls (grow-only)
+  size_t whole_bytes = 0;
 };
 
 DevState g_dev[kMaxDevices];
@@ -819,17 +822,21 @@ int run_views(int dtype, int out_dtype, int mask_kind, const View& Q, const View
                                                    (d.Nq - 1) * d.mask_stride[2] + d.Nk)
                              : 0;
     const size_t ln = d.lse ? sizeof(float) * d.B * d.Hq * d.Nq : 0;
-    char* buf = nullptr;
     const size_t total = qn + kn + vn + on + mn + ln + 6 * 256;
-    CUDA_TRY(cudaMalloc(&buf, total));
+    DevState& st = g_dev[dev];
+    // One staged call per device at a time; the buffer is kept for the next.
+    std::lock_guard<std::mutex> lk(st.whole_mu);
+    if ((rc = ensure(&st.whole, &st.whole_bytes, total)) != ATTN_OK) return rc;
+    char* buf = static_cast<char*>(st.whole);
     auto carve = [&](size_t n) { char* p = buf; buf += (n + 255) / 256 * 256; return p; };
-    char* base = buf;
     char* dq = carve(qn); char* dk = carve(kn); char* dv = carve(vn); char* dout = carve(on);
     char* dm = mn ? carve(mn) : nullptr;
     char* dl = ln ? carve(ln) : nullptr;
-    DevState& st = g_dev[dev];
     cudaStream_t s = st.s_compute;
-    auto cleanup = [&](int code) { cudaFree(base); return code; };
+    auto cleanup = [&](int code) {
+      if (code != ATTN_OK) cudaStreamSynchronize(s);  // nothing may still use the buffer
+      return code;
+    };
     if (cudaMemcpyAsync(dq, d.q, qn, cudaMemcpyHostToDevice, s) != cudaSuccess ||
         cudaMemcpyAsync(dk, d.k, kn, cudaMemcpyHostToDevice, s) != cudaSuccess ||
         cudaMemcpyAsync(dv, d.v, vn, cudaMemcpyHostToDevice, s) != cudaSuccess ||
