@@ -33,6 +33,7 @@ struct F32Params {
   int Hq, group, Nq, Nk, D;
   int mask_kind;  // 0 none, 1 causal, 2 dense
   float scale;
+  int vec4;       // 1: K/V rows are 16-byte aligned with D % 4 == 0 (float4 staging)
 };
 
 constexpr int kRows = 4;
@@ -75,12 +76,39 @@ __global__ void __launch_bounds__(kRows * 32)
   }
   for (int k0 = 0; k0 < kend; k0 += kChunk) {
     __syncthreads();
-    for (int idx = threadIdx.x; idx < kChunk * D; idx += blockDim.x) {
-      const int kr = idx / D, d = idx - (idx / D) * D;
-      const int key = k0 + kr;
-      const bool in = key < p.Nk;
-      sK[kr * (DMAX + 1) + d] = in ? K[key * p.k_sn + d] : 0.f;
-      sV[kr * DMAX + d] = in ? V[key * p.v_sn + d] : 0.f;
+    if (p.vec4) {
+      // 16-byte loads, all of a thread's loads issued before any store.
+      const int D4 = D >> 2;
+      constexpr int kPer = (kChunk * DMAX / 4 + kRows * 32 - 1) / (kRows * 32);
+      float4 kv[kPer], vv[kPer];
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int idx = threadIdx.x + u * kRows * 32;
+        const int kr = idx / D4, d4 = idx - (idx / D4) * D4;
+        const int key = k0 + kr;
+        const bool in = idx < kChunk * D4 && key < p.Nk;
+        kv[u] = in ? __ldg(reinterpret_cast<const float4*>(K + key * p.k_sn) + d4)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        vv[u] = in ? __ldg(reinterpret_cast<const float4*>(V + key * p.v_sn) + d4)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int idx = threadIdx.x + u * kRows * 32;
+        if (idx >= kChunk * D4) break;
+        const int kr = idx / D4, d = (idx - (idx / D4) * D4) * 4;
+        float* k_dst = sK + kr * (DMAX + 1) + d;  // padded rows: scalar stores
+        k_dst[0] = kv[u].x; k_dst[1] = kv[u].y; k_dst[2] = kv[u].z; k_dst[3] = kv[u].w;
+        *reinterpret_cast<float4*>(sV + kr * DMAX + d) = vv[u];
+      }
+    } else {
+      for (int idx = threadIdx.x; idx < kChunk * D; idx += blockDim.x) {
+        const int kr = idx / D, d = idx - (idx / D) * D;
+        const int key = k0 + kr;
+        const bool in = key < p.Nk;
+        sK[kr * (DMAX + 1) + d] = in ? K[key * p.k_sn + d] : 0.f;
+        sV[kr * DMAX + d] = in ? V[key * p.v_sn + d] : 0.f;
+      }
     }
     __syncthreads();
     const int key = k0 + lane;

@@ -355,6 +355,10 @@ int launch_f32(const AttnDesc& d, cudaStream_t stream) {
   p.D = static_cast<int>(d.D);
   p.mask_kind = d.mask_kind;
   p.scale = d.scale;
+  p.vec4 = (d.D % 4 == 0 && d.k_stride[2] % 4 == 0 && d.v_stride[2] % 4 == 0 &&
+            d.k_stride[1] % 4 == 0 && d.v_stride[1] % 4 == 0 && d.k_stride[0] % 4 == 0 &&
+            d.v_stride[0] % 4 == 0 && (reinterpret_cast<uintptr_t>(d.k) & 15u) == 0 &&
+            (reinterpret_cast<uintptr_t>(d.v) & 15u) == 0) ? 1 : 0;
   dim3 grid(static_cast<unsigned>((d.Nq + attn_f32::kRows - 1) / attn_f32::kRows),
             static_cast<unsigned>(d.B * d.Hq));
   kern<<<grid, attn_f32::kRows * 32, smem, stream>>>(p);
