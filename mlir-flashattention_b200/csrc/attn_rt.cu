@@ -325,6 +325,58 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
   return ATTN_OK;
 }
 
+// fp32, head_dim 64 or 128 with every operand row 16-byte aligned: the
+// register-tiled kernel.
+template <int D>
+int launch_f32_tiled(const AttnDesc& d, cudaStream_t stream) {
+  auto kern = attn_f32::attn_fwd_f32_tiled<D>;
+  constexpr size_t smem = attn_f32::f32_tiled_smem_bytes<D>();
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem));
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute");
+  attn_f32::F32Params p{};
+  p.q = static_cast<const float*>(d.q);
+  p.k = static_cast<const float*>(d.k);
+  p.v = static_cast<const float*>(d.v);
+  p.o = static_cast<float*>(d.o);
+  p.lse = d.lse;
+  p.mask = d.mask;
+  p.q_sb = d.q_stride[0]; p.q_sh = d.q_stride[1]; p.q_sn = d.q_stride[2];
+  p.k_sb = d.k_stride[0]; p.k_sh = d.k_stride[1]; p.k_sn = d.k_stride[2];
+  p.v_sb = d.v_stride[0]; p.v_sh = d.v_stride[1]; p.v_sn = d.v_stride[2];
+  p.o_sb = d.o_stride[0]; p.o_sh = d.o_stride[1]; p.o_sn = d.o_stride[2];
+  p.m_sb = d.mask_stride[0]; p.m_sh = d.mask_stride[1]; p.m_sn = d.mask_stride[2];
+  p.Hq = static_cast<int>(d.Hq);
+  p.group = static_cast<int>(d.Hq / d.Hkv);
+  p.Nq = static_cast<int>(d.Nq);
+  p.Nk = static_cast<int>(d.Nk);
+  p.D = D;
+  p.mask_kind = d.mask_kind;
+  p.scale = d.scale;
+  p.vec4 = 1;
+  dim3 grid(static_cast<unsigned>((d.Nq + attn_f32::kTBM - 1) / attn_f32::kTBM),
+            static_cast<unsigned>(d.B * d.Hq));
+  kern<<<grid, attn_f32::kTThreads, smem, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_f32_tiled launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return ATTN_OK;
+}
+
+// Rows of Q, K, V and O start on 16-byte boundaries (float4 access).
+bool f32_rows_aligned(const AttnDesc& d) {
+  auto ok = [](const void* p, const int64_t* st) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && st[0] % 4 == 0 && st[1] % 4 == 0 &&
+           st[2] % 4 == 0;
+  };
+  return ok(d.q, d.q_stride) && ok(d.k, d.k_stride) && ok(d.v, d.v_stride) &&
+         ok(d.o, d.o_stride);
+}
+
 template <int DMAX>
 int launch_f32(const AttnDesc& d, cudaStream_t stream) {
   auto kern = attn_f32::attn_fwd_f32_kernel<DMAX>;
@@ -512,6 +564,8 @@ int dispatch_mode(const AttnDesc& d, int32_t* status, cudaStream_t s) {
 
 int dispatch(const AttnDesc& d, int32_t* status, cudaStream_t s) {
   if (d.dtype == ATTN_F32) {
+    if ((d.D == 64 || d.D == 128) && f32_rows_aligned(d))
+      return d.D == 64 ? launch_f32_tiled<64>(d, s) : launch_f32_tiled<128>(d, s);
     if (d.D <= 64) return launch_f32<64>(d, s);
     if (d.D <= 128) return launch_f32<128>(d, s);
     return launch_f32<256>(d, s);

@@ -546,3 +546,38 @@ def test_long_causal_sequence_sampled_tiles(pkg, oracle):
         rows = slice(t * 128, t * 128 + 128)
         assert _rel(got[0, 0, rows], ref[0, 0, rows]) <= 2e-2, t
         assert np.abs(lse[0, 0, rows] - ref_lse[0, 0, rows]).max() <= 1e-3, t
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("kind", ["none", "causal", "dense"])
+def test_f32_tiled_parity(pkg, oracle, D, kind):
+    """fp32 with head_dim 64 / 128 (the register-tiled CUDA-core kernel):
+    ragged Nq / Nk, grouped heads, at the reference op's 1e-4 tolerance; dense
+    masks include rows masked over keys [0, 128) only (NaN in the reference)."""
+    rng = np.random.default_rng(D + len(kind))
+    B, Hq, Hkv, Nq, Nk = 2, 4, 2, 333, 517
+    if kind == "causal":
+        Nk = Nq
+    q = rng.standard_normal((B, Hq, Nq, D)).astype(np.float32)
+    k = rng.standard_normal((B, Hkv, Nk, D)).astype(np.float32)
+    v = rng.standard_normal((B, Hkv, Nk, D)).astype(np.float32)
+    M = None
+    if kind == "dense":
+        M = rng.random((B, Hq, Nq, Nk)) < 0.3
+        M[..., 0] = False
+        M[0, 1, [7, 100], :128] = True
+        M[1, 3, 200, :] = True
+    L = torch.empty((B, Hq, Nq), dtype=torch.float32, device="cuda")
+    out = pkg.fused(*(torch.from_numpy(a).cuda() for a in (q, k, v)), D ** -0.5,
+                    causal=kind == "causal", lse=L,
+                    mask=None if M is None else torch.from_numpy(M).cuda())
+    pkg.check_status(0)
+    ref, ref_lse = oracle.attn_batched(q, k, v, D ** -0.5, causal=kind == "causal", mask=M)
+    got, lse = out.cpu().numpy(), L.cpu().numpy()
+    assert (np.isnan(got) == np.isnan(ref)).all() and (np.isnan(lse) == np.isnan(ref_lse)).all()
+    ok = ~np.isnan(ref)
+    assert np.abs(got[ok] - ref[ok]).max() / np.abs(ref[ok]).max() <= 1e-4
+    okl = ~np.isnan(ref_lse)
+    assert np.abs(lse[okl] - ref_lse[okl]).max() <= 1e-4
+    if kind == "dense":
+        assert np.isnan(ref[0, 1, [7, 100]]).all() and np.isnan(ref[1, 3, 200]).all()
