@@ -353,13 +353,17 @@ def main():
         torch.cuda.synchronize(dev)
         ms = ev0.elapsed_time(ev1)
     else:
-        # Inputs fit in L2: write a 256 MB buffer before every step, outside
-        # that step's pair of events, so no step starts with a warm L2.
+        # Operands fit in L2: write a 256 MB buffer before every step, outside
+        # that step's pair of events, so no step starts with a warm L2.  A
+        # short device-side wait after the flush lets the host enqueue the
+        # step before its start event is reached, so the host's launch time
+        # is not counted as GPU time.
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.steps)]
         for a, b in evs:
             flush.zero_()
+            torch.cuda._sleep(200_000)  # ~0.1 ms of GPU clock cycles
             a.record(stream)
             step()
             b.record(stream)
