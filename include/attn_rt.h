@@ -30,6 +30,7 @@
 #ifndef ATTN_RT_H
 #define ATTN_RT_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -137,6 +138,17 @@ ATTN_API int attn_rt_version(void);
 
 /* Number of kernel launches attn_fwd issued in this process (all devices). */
 ATTN_API int64_t attn_rt_launch_count(void);
+
+/* Device memory helpers for callers that keep operands resident across calls
+ * (a lowered program that copies its memrefs to the GPU once and passes
+ * device memrefs to the entries below, instead of host memrefs that are
+ * staged on every call).  The allocation is on the current device, 256-byte
+ * aligned; `bytes` must be positive.  attn_rt_copy copies `bytes` between any
+ * two host or device addresses: asynchronously on `stream` when it is
+ * non-null, else synchronously. */
+ATTN_API int attn_rt_alloc(void** ptr, size_t bytes);
+ATTN_API int attn_rt_free(void* ptr);
+ATTN_API int attn_rt_copy(void* dst, const void* src, size_t bytes, void* stream);
 
 /* ---- MLIR memref-descriptor interface ------------------------------------
  * MLIR passes a memref<...> to an `llvm.emit_c_interface` function as a pointer

@@ -105,6 +105,13 @@ def lib():
         L.attn_rt_launch_count.restype = ctypes.c_int64
         L.attn_rt_probe_timeout.restype = ctypes.c_int
         L.attn_rt_probe_timeout.argtypes = [ctypes.c_int64]
+        L.attn_rt_alloc.restype = ctypes.c_int
+        L.attn_rt_alloc.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_size_t]
+        L.attn_rt_free.restype = ctypes.c_int
+        L.attn_rt_free.argtypes = [ctypes.c_void_p]
+        L.attn_rt_copy.restype = ctypes.c_int
+        L.attn_rt_copy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                   ctypes.c_void_p]
         m2, m4 = ctypes.POINTER(AttnMemRef2D), ctypes.POINTER(AttnMemRef4D)
         f = ctypes.c_float
         for name in ("nomask", "causal"):

@@ -926,6 +926,33 @@ int attn_rt_version(void) { return (1 << 16) | 1; }
 
 int64_t attn_rt_launch_count(void) { return g_launches.load(); }
 
+int attn_rt_alloc(void** ptr, size_t bytes) {
+  if (!ptr || bytes == 0) return fail(ATTN_ERR_INVALID, "attn_rt_alloc: null pointer or 0 bytes");
+  *ptr = nullptr;
+  int dev = 0, rc;
+  if ((rc = current_device(&dev)) != ATTN_OK) return rc;
+  if ((rc = init_device(dev)) != ATTN_OK) return rc;
+  CUDA_TRY(cudaMalloc(ptr, bytes));
+  return ATTN_OK;
+}
+
+int attn_rt_free(void* ptr) {
+  if (!ptr) return ATTN_OK;
+  CUDA_TRY(cudaFree(ptr));
+  return ATTN_OK;
+}
+
+int attn_rt_copy(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return ATTN_OK;
+  if (!dst || !src) return fail(ATTN_ERR_INVALID, "attn_rt_copy: null pointer");
+  if (stream) {
+    CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)));
+  } else {
+    CUDA_TRY(cudaMemcpy(dst, src, bytes, cudaMemcpyDefault));
+  }
+  return ATTN_OK;
+}
+
 const char* attn_rt_last_error(void) { return g_last_error.c_str(); }
 
 const char* attn_rt_status_string(int code) {

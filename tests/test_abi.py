@@ -92,3 +92,18 @@ def test_no_device_is_reported_not_faked(pkg):
         pytest.skip("a GPU is present")
     d = _desc(pkg)
     assert pkg.lib().attn_fwd(ctypes.byref(d), None) == -9
+
+
+def test_device_memory_helpers_without_a_gpu(pkg):
+    """attn_rt_alloc / free / copy check their arguments before any device
+    call, and report a missing GPU instead of faking memory."""
+    torch = pytest.importorskip("torch")
+    L = pkg.lib()
+    p = ctypes.c_void_p()
+    assert L.attn_rt_alloc(None, 16) == -1
+    assert L.attn_rt_alloc(ctypes.byref(p), 0) == -1
+    assert L.attn_rt_free(None) == 0
+    assert L.attn_rt_copy(None, None, 0, None) == 0
+    assert L.attn_rt_copy(None, ctypes.byref(p), 8, None) == -1
+    if not torch.cuda.is_available():
+        assert L.attn_rt_alloc(ctypes.byref(p), 256) == -9

@@ -581,3 +581,43 @@ def test_f32_tiled_parity(pkg, oracle, D, kind):
     assert np.abs(lse[okl] - ref_lse[okl]).max() <= 1e-4
     if kind == "dense":
         assert np.isnan(ref[0, 1, [7, 100]]).all() and np.isnan(ref[1, 3, 200]).all()
+
+
+def test_device_resident_memrefs_via_runtime_helpers(pkg, wl):
+    """A lowered program that keeps its operands on the GPU: attn_rt_alloc +
+    attn_rt_copy, then the memref entry on device memrefs, gives the same bits
+    as the host-memref call."""
+    import ctypes
+
+    w = wl.Workload("t", "bf16", 1, 4, 4, 300, 128, True, seed=23)
+    inp = wl.make_inputs(w)
+    q, k, v = (t.cpu().contiguous() for t in wl.to_device(inp, w))
+    ho = torch.empty_like(q)
+    L = pkg.lib()
+    lse0 = torch.empty((0, 0, 0, 1), dtype=torch.float32)
+    rc = L._mlir_ciface_attn_fused_bf16_causal_4d(pkg.memref(q), pkg.memref(k), pkg.memref(v),
+                                                  w.scale, pkg.memref(ho), pkg.memref(lse0))
+    assert rc == 0, pkg.last_error()
+    nbytes = q.numel() * 2
+    ptrs = []
+    for t in (q, k, v, ho):
+        p = ctypes.c_void_p()
+        assert L.attn_rt_alloc(ctypes.byref(p), nbytes) == 0, pkg.last_error()
+        ptrs.append(p.value)
+    for src, dst in zip((q, k, v), ptrs):
+        assert L.attn_rt_copy(dst, src.data_ptr(), nbytes, None) == 0
+
+    def dev_memref(ptr, like):
+        m = pkg.memref(like)
+        m.allocated = m.aligned = ptr
+        return m
+
+    rc = L._mlir_ciface_attn_fused_bf16_causal_4d(
+        dev_memref(ptrs[0], q), dev_memref(ptrs[1], k), dev_memref(ptrs[2], v), w.scale,
+        dev_memref(ptrs[3], ho), pkg.memref(lse0))
+    assert rc == 0, pkg.last_error()
+    back = torch.empty_like(ho)
+    assert L.attn_rt_copy(back.data_ptr(), ptrs[3], nbytes, None) == 0
+    for p in ptrs:
+        assert L.attn_rt_free(p) == 0
+    assert torch.equal(back, ho)
