@@ -1010,6 +1010,18 @@ int attn_fwd(const AttnDesc* desc, void* stream) {
   int dev = 0;
   if ((rc = current_device(&dev)) != ATTN_OK) return rc;
   if ((rc = init_device(dev)) != ATTN_OK) return rc;
+  {
+    // Kernels read these with TMA and plain loads: host memory would fault.
+    const AttnDesc& d = *desc;
+    const void* need[] = {no_keys ? nullptr : d.q, no_keys ? nullptr : d.k,
+                          no_keys ? nullptr : d.v, d.o, d.lse, d.mask, d.q_descale_blocks,
+                          d.k_descale_blocks, d.v_descale_heads};
+    for (const void* ptr : need)
+      if (ptr && !is_device_ptr(ptr))
+        return fail(ATTN_ERR_INVALID,
+                    "attn_fwd takes device pointers; host buffers go through the memref "
+                    "entries or attn_fwd_host_noalloc");
+  }
   if (no_keys) {
     const AttnDesc& d = *desc;
     const int64_t rows = d.B * d.Hq * d.Nq;

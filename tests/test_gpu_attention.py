@@ -621,3 +621,28 @@ def test_device_resident_memrefs_via_runtime_helpers(pkg, wl):
     for p in ptrs:
         assert L.attn_rt_free(p) == 0
     assert torch.equal(back, ho)
+
+
+def test_attn_fwd_rejects_host_pointers(pkg, wl):
+    """The descriptor entry takes device pointers: a host buffer is refused
+    before any launch (no fault), and the next call runs normally."""
+    import ctypes
+
+    w = wl.Workload("t", "bf16", 1, 2, 2, 256, 128, False, seed=3)
+    inp = wl.make_inputs(w)
+    q, k, v = wl.to_device(inp, w)
+    out = torch.empty_like(q)
+    host_k = k.cpu()
+    d = pkg.AttnDesc()
+    d.dtype, d.out_dtype, d.mask_kind = pkg.ATTN_BF16, pkg.ATTN_BF16, pkg.MASK_NONE
+    d.B, d.Hq, d.Hkv, d.Nq, d.Nk, d.D = 1, 2, 2, 256, 256, 128
+    for dst, t in ((d.q_stride, q), (d.k_stride, k), (d.v_stride, v), (d.o_stride, out)):
+        dst[0], dst[1], dst[2] = t.stride(0), t.stride(1), t.stride(2)
+    d.q, d.k, d.v, d.o = q.data_ptr(), host_k.data_ptr(), v.data_ptr(), out.data_ptr()
+    d.scale = w.scale
+    d.q_descale = d.k_descale = d.v_descale = 1.0
+    rc = pkg.lib().attn_fwd(ctypes.byref(d), torch.cuda.current_stream().cuda_stream)
+    assert rc == -1 and "device pointers" in pkg.last_error()
+    ref = pkg.fused(q, k, v, w.scale)
+    pkg.check_status(0)
+    assert torch.isfinite(ref.float()).all()
