@@ -646,3 +646,23 @@ def test_attn_fwd_rejects_host_pointers(pkg, wl):
     ref = pkg.fused(q, k, v, w.scale)
     pkg.check_status(0)
     assert torch.isfinite(ref.float()).all()
+
+
+@pytest.mark.parametrize("in_dt", ["bf16", "f16"])
+@pytest.mark.parametrize("out_dt", ["bf16", "f16", "f32"])
+def test_input_output_type_matrix(pkg, oracle, in_dt, out_dt):
+    """Every input / output element type pair of the tensor-core kernel
+    (causal, grouped heads, ragged N)."""
+    tin = {"bf16": torch.bfloat16, "f16": torch.float16}[in_dt]
+    tout = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[out_dt]
+    g = torch.Generator(device="cuda").manual_seed(40 + len(in_dt) + len(out_dt))
+    B, Hq, Hkv, N, D = 1, 4, 2, 300, 128
+    q = torch.randn((B, Hq, N, D), generator=g, device="cuda").to(tin)
+    k = torch.randn((B, Hkv, N, D), generator=g, device="cuda").to(tin)
+    v = torch.randn((B, Hkv, N, D), generator=g, device="cuda").to(tin)
+    out = torch.empty((B, Hq, N, D), dtype=tout, device="cuda")
+    pkg.fused(q, k, v, D ** -0.5, output=out, causal=True)
+    pkg.check_status(0)
+    ref, _ = oracle.attn_batched(*(t.float().cpu().numpy() for t in (q, k, v)), D ** -0.5,
+                                 causal=True)
+    assert _rel(out.float().cpu().numpy(), ref) <= 2e-2
