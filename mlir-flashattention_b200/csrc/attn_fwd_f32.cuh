@@ -176,7 +176,7 @@ constexpr int kTBM = 64, kTBN = 64, kTThreads = 128;
 
 template <int D>
 constexpr size_t f32_tiled_smem_bytes() {
-  return sizeof(float) * (D * kTBM + D * kTBN + kTBN * D + kTBM * (kTBN + 4));
+  return sizeof(float) * (D * kTBM + D * kTBN + kTBN * D + kTBM * (kTBN + 1));
 }
 
 template <int D>
@@ -187,8 +187,10 @@ __global__ void __launch_bounds__(kTThreads)
   float* sQt = reinterpret_cast<float*>(smem4);  // [D][64]
   float* sKt = sQt + D * kTBM;                    // [D][64]
   float* sV = sKt + D * kTBN;                     // [64][D]
-  float* sP = sV + kTBN * D;                      // [64][64 + 4]
-  constexpr int PLD = kTBN + 4;
+  float* sP = sV + kTBN * D;                      // [64][64 + 1]
+  // Row pitch 65: the two row groups a warp reads in the P·V loop (8 rows
+  // apart) fall in different banks.
+  constexpr int PLD = kTBN + 1;
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int bh = blockIdx.y;
   const int b = bh / p.Hq, h = bh - (bh / p.Hq) * p.Hq, hk = h / p.group;
@@ -290,8 +292,8 @@ __global__ void __launch_bounds__(kTThreads)
 #pragma unroll
       for (int c = 0; c < TN; ++c) o[i][c] *= alpha;
       m[i] = m_new;
-      *reinterpret_cast<float4*>(sP + (ty * 8 + i) * PLD + tx * 4) =
-          make_float4(sc[i][0], sc[i][1], sc[i][2], sc[i][3]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sP[(ty * 8 + i) * PLD + tx * 4 + j] = sc[i][j];
     }
     __syncthreads();
 #pragma unroll 2
