@@ -666,3 +666,28 @@ def test_input_output_type_matrix(pkg, oracle, in_dt, out_dt):
     ref, _ = oracle.attn_batched(*(t.float().cpu().numpy() for t in (q, k, v)), D ** -0.5,
                                  causal=True)
     assert _rel(out.float().cpu().numpy(), ref) <= 2e-2
+
+
+@pytest.mark.parametrize("scale", [-0.09, 0.0])
+@pytest.mark.parametrize("kind", ["causal", "dense"])
+def test_negative_and_zero_scale(pkg, oracle, scale, kind):
+    """The op's scale is any f32: a negative scale flips which score is the
+    row maximum (the kernel reduces with min then), zero gives uniform weights
+    over the visible keys."""
+    g = torch.Generator(device="cuda").manual_seed(50)
+    B, H, N, D = 1, 2, 400, 128
+    q, k, v = (torch.randn((B, H, N, D), generator=g, device="cuda").to(torch.bfloat16)
+               for _ in range(3))
+    M = None
+    if kind == "dense":
+        M = torch.rand((N, N), generator=g, device="cuda") < 0.3
+        M[:, 0] = False
+    L = torch.empty((B, H, N), dtype=torch.float32, device="cuda")
+    out = pkg.fused(q, k, v, scale, causal=kind == "causal", mask=M, lse=L, classify=False)
+    pkg.check_status(0)
+    ref, ref_lse = oracle.attn_batched(*(t.float().cpu().numpy() for t in (q, k, v)), scale,
+                                       causal=kind == "causal",
+                                       mask=None if M is None else np.broadcast_to(
+                                           M.cpu().numpy(), (B, H, N, N)))
+    assert _rel(out.float().cpu().numpy(), ref) <= 2e-2
+    assert np.abs(L.cpu().numpy() - ref_lse).max() <= 1e-3
