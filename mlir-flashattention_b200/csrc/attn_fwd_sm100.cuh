@@ -505,8 +505,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Tile t's next softmax then overlaps the other tile's GEMMs.
         bool first_pv[2] = {true, true};
         int i = 0;  // position of kt in this pair's KV tile list
+        int kn_ahead = DENSE ? sc.next(kt0) : 0;
         for (int kt = kt0; kt < kt_end && ok; ++i) {
-          const int kn = sc.next(kt);
+          const int kn = DENSE ? kn_ahead : sc.next(kt);
+          // Dense masks: every class lookup of this step up front, before any
+          // wait, so none sits between a P·V issue and the S issue behind it
+          // (no-mask and causal lookups are arithmetic and stay inline).
+          int kn2 = 0;
+          bool act_kt[2] = {false, false}, act_kn[2] = {false, false};
+          if constexpr (DENSE) {
+            kn2 = kn < kt_end ? sc.next(kn) : kt_end;
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              act_kt[t] = sc.act(t, kt);
+              act_kn[t] = kn < kt_end && sc.act(t, kn);
+            }
+          }
           bool k_next = false;
           auto wait_k_next = [&]() {
             if (!k_next) k_next = wait(&kv_full[kst(i + 1)], kph(i + 1));
@@ -517,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           for (int t = 0; t < 2 && ok; ++t) {
-            if (!sc.act(t, kt)) continue;
+            if (!(DENSE ? act_kt[t] : sc.act(t, kt))) continue;
             if (!wait(&p_ready[t], p_cnt[t])) {
               ok = false;
               break;
@@ -534,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             first_pv[t] = false;
             mma_commit_lead(lead, &pv_done[t]);
             ++pv_cnt[t];
-            if (kn < kt_end && sc.act(t, kn)) {
+            if (DENSE ? act_kn[t] : (kn < kt_end && sc.act(t, kn))) {
               if (!wait_k_next()) {
                 ok = false;
                 break;
@@ -548,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (DENSE) {
             // A Q tile that skipped kt but needs kn gets its S GEMM here.
             for (int t = 0; t < 2 && ok; ++t) {
-              if (kn >= kt_end || sc.act(t, kt) || !sc.act(t, kn)) continue;
+              if (act_kt[t] || !act_kn[t]) continue;
               if (!wait_k_next()) {
                 ok = false;
                 break;
@@ -566,9 +580,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             mma_commit_lead(lead, &kv_empty[kst(i + 1)]);  // K free once its S GEMMs finish
-            if (sc.next(kn) >= kt_end) mma_commit_lead(lead, q_empty);
+            if ((DENSE ? kn2 : sc.next(kn)) >= kt_end) mma_commit_lead(lead, q_empty);
           }
           kt = kn;
+          kn_ahead = kn2;
         }
         for (int t = 0; t < 2; ++t)
           if (sc.any(t)) ++items_t[t];
@@ -912,8 +927,7 @@ __global__ void __launch_bounds__(kClassifyWarps * 32)
 // the causal mode's fixed order does.  One CTA: weights, a counting sort over
 // at most kOrderBuckets weights (more: the slice-major identity order),
 // scatter.
-// Items of equal weight may land in any order; each item is computed the
-// same way wherever it lands.
+// Items of equal weight keep their slice-major order.
 constexpr int kOrderBuckets = 4096;
 
 __global__ void __launch_bounds__(1024)
@@ -954,7 +968,30 @@ __global__ void __launch_bounds__(1024)
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < items; i += blockDim.x) order[atomicAdd(&start[weight[i]], 1)] = i;
+  // Stable scatter (equal weights keep the slice-major order, so the result
+  // and the schedule are the same on every call): a chunk of blockDim items at
+  // a time, warps in turn, each weight group of a warp placed by its leader.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  for (int c0 = 0; c0 < items; c0 += blockDim.x) {
+    const int i = c0 + static_cast<int>(threadIdx.x);
+    const bool valid = i < items;
+    const int wgt = valid ? static_cast<int>(weight[i]) : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, wgt);
+    const int leader = __ffs(same) - 1;
+    const int rank = __popc(same & ((1u << lane) - 1u));
+    for (int wj = 0; wj < nwarps; ++wj) {
+      if (warp == wj) {
+        int base = 0;
+        if (lane == leader && valid) {
+          base = start[wgt];
+          start[wgt] = base + __popc(same);
+        }
+        base = __shfl_sync(0xffffffffu, base, leader);
+        if (valid) order[base + rank] = i;
+      }
+      __syncthreads();
+    }
+  }
 }
 
 }  // namespace attn_sm100
