@@ -18,11 +18,15 @@
 //               P·V_0(j), S_0(j'), P·V_1(j), S_1(j') where j' is the next
 //               KV tile of the pair's list (PairSched); each S GEMM follows
 //               the P·V GEMM reading the same TMEM columns in issue order.
+//               d = 64 ("early S", P in columns of its own): S_0(j'), S_1(j')
+//               as soon as each softmax has read its S, then P·V_0(j),
+//               P·V_1(j).
 //   warps 0-3   softmax for Q tile 0, warps 4-7 for Q tile 1: one thread per
 //               query row reads its S row from TMEM, applies the mask, updates
 //               (m, l) in registers, writes P (bf16 / f16 / e4m3) back into the
-//               S columns and rescales its O row in TMEM when m moved; at the
-//               end of a pair it writes O / l and the LSE.
+//               S columns (d = 64: P's own columns) and rescales its O row in
+//               TMEM when m moved; at the end of a pair it writes O / l and
+//               the LSE.
 //   warps 10-11 idle (they complete warpgroup 2 for the register split).
 //   The two Q tiles ping-pong: while one softmax group works, the tensor
 //   cores run the other tile's GEMMs.  Registers: launched at 168 per thread
@@ -30,7 +34,7 @@
 //   theirs to 224 and warpgroup 2 lowers its to 56 (setmaxnreg).
 //
 // TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,256+D)
-// O1 [256+D, 256+2D).  Exponentials are base 2 with the scale folded in:
+// O1 [256+D, 256+2D); at d = 64 P0 [384,448) P1 [448,512).  Exponentials are base 2 with the scale folded in:
 // p = 2^(s·scale·log2e − m).  The running max only moves when it grows by
 // more than 2^8 (values of p stay <= 256, exact in bf16/e4m3 range), which
 // skips most O rescales; the final O/l and LSE are unaffected by the choice.
@@ -118,8 +122,12 @@ struct FwdCfg {
   // Operand format field: kind::f16 has F16 = 0, BF16 = 1; kind::f8f6f4 E4M3 = 0.
   static constexpr uint32_t kFmt = ELT == kEltBF16 ? 1u : 0u;
   static constexpr int kKind = FP8 ? 1 : 0;
-  static constexpr int kPCols = 128 * kEB / 4;          // TMEM columns holding P
-  static constexpr int kNumBars = 2 + 2 * kStages + 2 + 2 + 2 + 2 + 1;
+  // TMEM: S_t at columns 128 t, O_t at 256 + D t.  At d = 128 the columns
+  // are all taken and P_t overwrites S_t, so the next S_t GEMM follows the
+  // P·V GEMM; at d = 64, P_t has its own columns (384 + 64 t) and the next
+  // S_t GEMM starts as soon as the softmax has read S_t ("early S").
+  static constexpr bool kEarlyS = D == 64 && !FP8;
+  static constexpr int kNumBars = 2 + 2 * kStages + 2 + 2 + 2 + 2 + 2 + 1;
   static constexpr size_t kSmemBytes =
       1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes + kNumBars * 8 + 16;
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
@@ -323,7 +331,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_ready = s_full + 2;
   uint64_t* pv_done = p_ready + 2;
   uint64_t* o_free = pv_done + 2;
-  uint64_t* drain = o_free + 2;
+  uint64_t* s_free = o_free + 2;  // early S: the softmax has read S_t
+  uint64_t* drain = s_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -345,6 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&p_ready[t], 4);  // one arrival per softmax warp
       mbar_init(&pv_done[t], 1);
       mbar_init(&o_free[t], 128);
+      mbar_init(&s_free[t], 4);  // one arrival per softmax warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -394,23 +404,33 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_4d(sQ + t * C::kTileBytes + c * C::kBoxBytes, &tmQ, q_full,
                           c * C::kBoxCols, itm.pair * 256 + 128 * t, h, b);
           ++qi;
-          for (; kt < kt_end && ok; kt = sc.next(kt)) {
+          auto load = [&](bool isv, int tile) {
+            const int s = ring % C::kStages;
+            const uint32_t u = static_cast<uint32_t>(ring / C::kStages);
+            if (!mbar_wait_bounded(&kv_empty[s], (u & 1u) ^ 1u, abort_flag, p.status,
+                                   kWaitLimitNs))
+              return false;
+            mbar_arrive_expect_tx(&kv_full[s], C::kTileBytes);
   #pragma unroll
-            for (int kv = 0; kv < 2; ++kv) {
-              const int s = ring % C::kStages;
-              const uint32_t u = static_cast<uint32_t>(ring / C::kStages);
-              if (!mbar_wait_bounded(&kv_empty[s], (u & 1u) ^ 1u, abort_flag, p.status,
-                                     kWaitLimitNs)) {
-                ok = false;
-                break;
-              }
-              mbar_arrive_expect_tx(&kv_full[s], C::kTileBytes);
-  #pragma unroll
-              for (int c = 0; c < C::kNBox; ++c)
-                tma_load_4d(sKV + s * C::kTileBytes + c * C::kBoxBytes, kv ? &tmV : &tmK,
-                            &kv_full[s], c * C::kBoxCols, kt * 128, hk, b);
-              ++ring;
+            for (int c = 0; c < C::kNBox; ++c)
+              tma_load_4d(sKV + s * C::kTileBytes + c * C::kBoxBytes, isv ? &tmV : &tmK,
+                          &kv_full[s], c * C::kBoxCols, tile * 128, hk, b);
+            ++ring;
+            return true;
+          };
+          if constexpr (C::kEarlyS) {
+            // The MMA warp's order: K(kt_0), then K(kt_i+1) ahead of V(kt_i),
+            // then V(kt_last).
+            ok = load(false, kt);
+            while (ok) {
+              const int kn = sc.next(kt);
+              if (kn < kt_end) ok = load(false, kn);
+              if (ok) ok = load(true, kt);
+              if (kn >= kt_end) break;
+              kt = kn;
             }
+          } else {
+            for (; kt < kt_end && ok; kt = sc.next(kt)) ok = load(false, kt) && load(true, kt);
           }
         }
         // Wait for every copy this thread started before the CTA may exit.
@@ -449,9 +469,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto issue_PV = [&](int t, int stage, bool acc) {
         const uint64_t b0 = dV0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
+        const uint32_t tP = tmem + (C::kEarlyS ? 384 + t * 64 : t * 128);  // P_t's columns
   #pragma unroll
         for (int kk = 0; kk < C::kKStepsPV; ++kk)
-          mma_ts_lead<C::kKind>(lead, tmem + 256 + t * D, tmem + t * 128 + kk * 8,
+          mma_ts_lead<C::kKind>(lead, tmem + 256 + t * D, tP + kk * 8,
                                 b0 + static_cast<uint64_t>((kk * C::kKeysPerStep * 128) >> 4), idO,
                                 (acc || kk > 0) ? 1u : 0u);
       };
@@ -461,6 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int ring = 0;             // ring position of this pair's K_0
       int qi = 0;               // pairs started
       int pv_cnt[2] = {0, 0};   // P·V GEMMs committed per tile (pv_done phases)
+      int s_cnt[2] = {0, 0};    // early S: S GEMMs issued per tile (s_free phases)
       int p_cnt[2] = {0, 0};    // p_ready phases consumed per tile
       int items_t[2] = {0, 0};  // pairs in which tile t was active
       bool ok = true;
@@ -472,118 +494,202 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kt_end = sc.end();
         const int kt0 = sc.next(-1);
         if (kt0 >= kt_end) continue;  // no KV tile (the producer skips the pair too)
-        // Ring slots of the i-th KV tile of this pair (K, then V).
-        auto kst = [&](int i) { return (ring + 2 * i) % C::kStages; };
-        auto kph = [&](int i) { return (ring + 2 * i) / C::kStages; };
-        auto vst = [&](int i) { return (ring + 2 * i + 1) % C::kStages; };
-        auto vph = [&](int i) { return (ring + 2 * i + 1) / C::kStages; };
-        if (!wait(q_full, qi) || !wait(&kv_full[kst(0)], kph(0))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (!sc.act(t, kt0)) continue;
-          // S_t's columns may still hold the previous pair's last P_t, read by
-          // a P·V GEMM issued earlier from this thread (see the ordering note
-          // below).
-          issue_S(t, kst(0));
-          mma_commit_lead(lead, &s_full[t]);
-        }
-        if (!ok) break;
-        mma_commit_lead(lead, &kv_empty[kst(0)]);  // K free once its S GEMMs finish
-        if (sc.next(kt0) >= kt_end) mma_commit_lead(lead, q_empty);  // all S GEMMs issued
-        // Per KV tile, for each Q tile t that needs it: O_t += P_t·V, then
-        // S_t = Q_t·Kᵀ of t's next KV tile right behind it.  P_t lives in the
-        // S_t columns; the S GEMM is issued without waiting for the P·V GEMM
-        // to complete because tcgen05.mma operations issued by one thread run
-        // through the tensor pipe in issue order, so the S GEMM's accumulator
-        // writes come after the P·V GEMM's reads of P_t.  (CUTLASS's SM100
-        // attention mainloop issues its S GEMM behind the P·V GEMM on the
-        // same columns the same way.  Waiting for P·V completion instead
-        // costs a pipe drain per tile step: 2-7 % measured, identical bits.)
-        // Tile t's next softmax then overlaps the other tile's GEMMs.
-        bool first_pv[2] = {true, true};
         int i = 0;  // position of kt in this pair's KV tile list
-        int kn_ahead = DENSE ? sc.next(kt0) : 0;
-        for (int kt = kt0; kt < kt_end && ok; ++i) {
-          const int kn = DENSE ? kn_ahead : sc.next(kt);
-          // Dense masks: every class lookup of this step up front, before any
-          // wait, so none sits between a P·V issue and the S issue behind it
-          // (no-mask and causal lookups are arithmetic and stay inline).
-          int kn2 = 0;
-          bool act_kt[2] = {false, false}, act_kn[2] = {false, false};
-          if constexpr (DENSE) {
-            kn2 = kn < kt_end ? sc.next(kn) : kt_end;
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              act_kt[t] = sc.act(t, kt);
-              act_kn[t] = kn < kt_end && sc.act(t, kn);
-            }
-          }
-          bool k_next = false;
-          auto wait_k_next = [&]() {
-            if (!k_next) k_next = wait(&kv_full[kst(i + 1)], kph(i + 1));
-            return k_next;
+        if constexpr (C::kEarlyS) {
+          // Ring positions (the producer's order): K of the first KV tile at
+          // `ring`, then for step i K of the next tile at ring + 2i + 1 ahead
+          // of V of this tile at ring + 2i + 2, the last V at ring + 2i + 1.
+          auto slot = [](int pos) { return pos % C::kStages; };
+          auto phs = [](int pos) { return pos / C::kStages; };
+          // S_t into its TMEM columns once the softmax has read the previous S_t.
+          auto issue_S_t = [&](int t, int kpos) {
+            if (s_cnt[t] > 0 && !wait(&s_free[t], s_cnt[t] - 1)) return false;
+            tc_fence_after();
+            issue_S(t, slot(kpos));
+            mma_commit_lead(lead, &s_full[t]);
+            ++s_cnt[t];
+            return true;
           };
-          if (!wait(&kv_full[vst(i)], vph(i))) {
+          if (!wait(q_full, qi) || !wait(&kv_full[slot(ring)], phs(ring))) {
             ok = false;
             break;
           }
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (!(DENSE ? act_kt[t] : sc.act(t, kt))) continue;
-            if (!wait(&p_ready[t], p_cnt[t])) {
-              ok = false;
-              break;
-            }
-            ++p_cnt[t];
-            // The first P·V GEMM of a pair overwrites O_t: the previous pair's
-            // epilogue must have read it.
-            if (first_pv[t] && items_t[t] > 0 && !wait(&o_free[t], items_t[t] - 1)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_PV(t, vst(i), !first_pv[t]);
-            first_pv[t] = false;
-            mma_commit_lead(lead, &pv_done[t]);
-            ++pv_cnt[t];
-            if (DENSE ? act_kn[t] : (kn < kt_end && sc.act(t, kn))) {
-              if (!wait_k_next()) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              issue_S(t, kst(i + 1));
-              mma_commit_lead(lead, &s_full[t]);
-            }
-          }
+          tc_fence_after();
+          for (int t = 0; t < 2 && ok; ++t)
+            if (sc.act(t, kt0)) ok = issue_S_t(t, ring);
           if (!ok) break;
-          if constexpr (DENSE) {
-            // A Q tile that skipped kt but needs kn gets its S GEMM here.
+          mma_commit_lead(lead, &kv_empty[slot(ring)]);  // K free once its S GEMMs finish
+          if (sc.next(kt0) >= kt_end) mma_commit_lead(lead, q_empty);  // all S GEMMs issued
+          // Per KV tile: the next tile's S GEMMs first (each needs only its
+          // softmax to have read the previous S), then O_t += P_t·V for each
+          // Q tile whose P is ready.
+          bool first_pv[2] = {true, true};
+          int kn_ahead = DENSE ? sc.next(kt0) : 0;
+          for (int kt = kt0; kt < kt_end && ok; ++i) {
+            const int kn = DENSE ? kn_ahead : sc.next(kt);
+            int kn2 = 0;
+            bool act_kt[2] = {false, false}, act_kn[2] = {false, false};
+            if constexpr (DENSE) {
+              kn2 = kn < kt_end ? sc.next(kn) : kt_end;
+#pragma unroll
+              for (int t = 0; t < 2; ++t) {
+                act_kt[t] = sc.act(t, kt);
+                act_kn[t] = kn < kt_end && sc.act(t, kn);
+              }
+            }
+            const bool more = kn < kt_end;
+            if (more) {
+              const int kpos = ring + 2 * i + 1;
+              if (!wait(&kv_full[slot(kpos)], phs(kpos))) {
+                ok = false;
+                break;
+              }
+              for (int t = 0; t < 2 && ok; ++t)
+                if (DENSE ? act_kn[t] : sc.act(t, kn)) ok = issue_S_t(t, kpos);
+              if (!ok) break;
+              mma_commit_lead(lead, &kv_empty[slot(kpos)]);
+              if ((DENSE ? kn2 : sc.next(kn)) >= kt_end) mma_commit_lead(lead, q_empty);
+            }
+            const int vpos = ring + 2 * i + (more ? 2 : 1);
+            if (!wait(&kv_full[slot(vpos)], phs(vpos))) {
+              ok = false;
+              break;
+            }
             for (int t = 0; t < 2 && ok; ++t) {
-              if (act_kt[t] || !act_kn[t]) continue;
-              if (!wait_k_next()) {
+              if (!(DENSE ? act_kt[t] : sc.act(t, kt))) continue;
+              if (!wait(&p_ready[t], p_cnt[t])) {
+                ok = false;
+                break;
+              }
+              ++p_cnt[t];
+              if (first_pv[t] && items_t[t] > 0 && !wait(&o_free[t], items_t[t] - 1)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              issue_S(t, kst(i + 1));
-              mma_commit_lead(lead, &s_full[t]);
+              issue_PV(t, slot(vpos), !first_pv[t]);
+              first_pv[t] = false;
+              mma_commit_lead(lead, &pv_done[t]);
             }
             if (!ok) break;
+            mma_commit_lead(lead, &kv_empty[slot(vpos)]);  // V free once the P·V GEMMs finish
+            kt = kn;
+            kn_ahead = kn2;
           }
-          mma_commit_lead(lead, &kv_empty[vst(i)]);  // V free once the P·V GEMMs finish
-          if (kn < kt_end) {
-            if (!wait_k_next()) {
+          if (!ok) break;
+        } else {
+          // Ring slots of the i-th KV tile of this pair (K, then V).
+          auto kst = [&](int i) { return (ring + 2 * i) % C::kStages; };
+          auto kph = [&](int i) { return (ring + 2 * i) / C::kStages; };
+          auto vst = [&](int i) { return (ring + 2 * i + 1) % C::kStages; };
+          auto vph = [&](int i) { return (ring + 2 * i + 1) / C::kStages; };
+          if (!wait(q_full, qi) || !wait(&kv_full[kst(0)], kph(0))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (!sc.act(t, kt0)) continue;
+            // S_t's columns may still hold the previous pair's last P_t, read by
+            // a P·V GEMM issued earlier from this thread (see the ordering note
+            // below).
+            issue_S(t, kst(0));
+            mma_commit_lead(lead, &s_full[t]);
+          }
+          if (!ok) break;
+          mma_commit_lead(lead, &kv_empty[kst(0)]);  // K free once its S GEMMs finish
+          if (sc.next(kt0) >= kt_end) mma_commit_lead(lead, q_empty);  // all S GEMMs issued
+          // Per KV tile, for each Q tile t that needs it: O_t += P_t·V, then
+          // S_t = Q_t·Kᵀ of t's next KV tile right behind it.  P_t lives in the
+          // S_t columns; the S GEMM is issued without waiting for the P·V GEMM
+          // to complete because tcgen05.mma operations issued by one thread run
+          // through the tensor pipe in issue order, so the S GEMM's accumulator
+          // writes come after the P·V GEMM's reads of P_t.  (CUTLASS's SM100
+          // attention mainloop issues its S GEMM behind the P·V GEMM on the
+          // same columns the same way.  Waiting for P·V completion instead
+          // costs a pipe drain per tile step: 2-7 % measured, identical bits.)
+          // Tile t's next softmax then overlaps the other tile's GEMMs.
+          bool first_pv[2] = {true, true};
+          int kn_ahead = DENSE ? sc.next(kt0) : 0;
+          for (int kt = kt0; kt < kt_end && ok; ++i) {
+            const int kn = DENSE ? kn_ahead : sc.next(kt);
+            // Dense masks: every class lookup of this step up front, before any
+            // wait, so none sits between a P·V issue and the S issue behind it
+            // (no-mask and causal lookups are arithmetic and stay inline).
+            int kn2 = 0;
+            bool act_kt[2] = {false, false}, act_kn[2] = {false, false};
+            if constexpr (DENSE) {
+              kn2 = kn < kt_end ? sc.next(kn) : kt_end;
+  #pragma unroll
+              for (int t = 0; t < 2; ++t) {
+                act_kt[t] = sc.act(t, kt);
+                act_kn[t] = kn < kt_end && sc.act(t, kn);
+              }
+            }
+            bool k_next = false;
+            auto wait_k_next = [&]() {
+              if (!k_next) k_next = wait(&kv_full[kst(i + 1)], kph(i + 1));
+              return k_next;
+            };
+            if (!wait(&kv_full[vst(i)], vph(i))) {
               ok = false;
               break;
             }
-            mma_commit_lead(lead, &kv_empty[kst(i + 1)]);  // K free once its S GEMMs finish
-            if ((DENSE ? kn2 : sc.next(kn)) >= kt_end) mma_commit_lead(lead, q_empty);
+            for (int t = 0; t < 2 && ok; ++t) {
+              if (!(DENSE ? act_kt[t] : sc.act(t, kt))) continue;
+              if (!wait(&p_ready[t], p_cnt[t])) {
+                ok = false;
+                break;
+              }
+              ++p_cnt[t];
+              // The first P·V GEMM of a pair overwrites O_t: the previous pair's
+              // epilogue must have read it.
+              if (first_pv[t] && items_t[t] > 0 && !wait(&o_free[t], items_t[t] - 1)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_PV(t, vst(i), !first_pv[t]);
+              first_pv[t] = false;
+              mma_commit_lead(lead, &pv_done[t]);
+              ++pv_cnt[t];
+              if (DENSE ? act_kn[t] : (kn < kt_end && sc.act(t, kn))) {
+                if (!wait_k_next()) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                issue_S(t, kst(i + 1));
+                mma_commit_lead(lead, &s_full[t]);
+              }
+            }
+            if (!ok) break;
+            if constexpr (DENSE) {
+              // A Q tile that skipped kt but needs kn gets its S GEMM here.
+              for (int t = 0; t < 2 && ok; ++t) {
+                if (act_kt[t] || !act_kn[t]) continue;
+                if (!wait_k_next()) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                issue_S(t, kst(i + 1));
+                mma_commit_lead(lead, &s_full[t]);
+              }
+              if (!ok) break;
+            }
+            mma_commit_lead(lead, &kv_empty[vst(i)]);  // V free once the P·V GEMMs finish
+            if (kn < kt_end) {
+              if (!wait_k_next()) {
+                ok = false;
+                break;
+              }
+              mma_commit_lead(lead, &kv_empty[kst(i + 1)]);  // K free once its S GEMMs finish
+              if ((DENSE ? kn2 : sc.next(kn)) >= kt_end) mma_commit_lead(lead, q_empty);
+            }
+            kt = kn;
+            kn_ahead = kn2;
           }
-          kt = kn;
-          kn_ahead = kn2;
         }
         for (int t = 0; t < 2; ++t)
           if (sc.any(t)) ++items_t[t];
@@ -604,6 +710,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quarter * 32 + lane;  // row within the tile == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tP = tmem + lane_off + (C::kEarlyS ? 384 + t * 64 : t * 128);
     const uint32_t tO = tmem + lane_off + 256 + t * D;
     const float sl2_base = p.scale_log2;  // scale·log2(e) (· per-tensor descales)
     const bool pos = sl2_base >= 0.f;      // descales are positive: the sign is scale's
@@ -702,6 +809,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             s[96 + i] = __uint_as_float(r3[i]);
           }
         }
+        if constexpr (C::kEarlyS) {
+          // S_t has been read: the next S GEMM of this tile may overwrite it.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[t]);
+        }
         const int kbase = kt * 128;
         if constexpr (DENSE) {
           if (sel) {
@@ -764,8 +877,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             pk[c] = ELT == kEltF16 ? pack_f16(s[2 * c], s[2 * c + 1])
                                    : pack_bf16(s[2 * c], s[2 * c + 1]);
           }
-          tmem_st32(tS + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
-          tmem_st32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+          if constexpr (C::kEarlyS) {
+            // P_t's columns and O_t: the previous P·V GEMM of this tile reads
+            // the one and accumulates into the other, so it must be complete
+            // before P_t is rewritten or O_t rescaled.  (Without early S the
+            // completion of this S GEMM, issued behind it, implies it.)
+            if (steps > 0 && !warp_wait(&pv_done[t], static_cast<uint32_t>((steps - 1) & 1),
+                                        abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+          tmem_st32(tP + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+          tmem_st32(tP + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
         } else {
           uint32_t pk[32];
 #pragma unroll
@@ -774,7 +899,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc1 = f2_add(acc1, f2_pack(s[4 * c + 2], s[4 * c + 3]));
             pk[c] = pack_e4m3x4(s[4 * c], s[4 * c + 1], s[4 * c + 2], s[4 * c + 3]);
           }
-          tmem_st32(tS + 0, pk);
+          tmem_st32(tP + 0, pk);
         }
         float q0, q1;
         f2_unpack(f2_add(acc0, acc1), q0, q1);
