@@ -286,14 +286,15 @@ def test_bf16_dense_block_sparse_mask(pkg, wl, oracle, D, broadcast):
     assert np.abs(lse[~nan_rows] - ref_lse[~nan_rows]).max() <= 1e-3
 
 
-def test_dense_causal_mask_equals_causal_variant(pkg, wl):
+@pytest.mark.parametrize("D", [64, 128])
+def test_dense_causal_mask_equals_causal_variant(pkg, wl, D):
     """A causal pattern given as an explicit i1 mask and run on the dense-mask
     path (every KV tile visited) gives the same bits as the causal
     specialisation, which skips the fully masked tiles: those tiles only add
     exact zeros."""
     import ctypes
 
-    w = wl.Workload("t", "bf16", 1, 4, 4, 640, 128, True, seed=8)
+    w = wl.Workload("t", "bf16", 1, 4, 4, 640, D, True, seed=8)
     inp = wl.make_inputs(w)
     q, k, v = wl.to_device(inp, w)
     a = pkg.fused(q, k, v, w.scale, causal=True)
@@ -301,7 +302,7 @@ def test_dense_causal_mask_equals_causal_variant(pkg, wl):
     out = torch.empty_like(a)
     d = pkg.AttnDesc()
     d.dtype, d.out_dtype, d.mask_kind = pkg.ATTN_BF16, pkg.ATTN_BF16, pkg.MASK_DENSE
-    d.B, d.Hq, d.Hkv, d.Nq, d.Nk, d.D = 1, 4, 4, 640, 640, 128
+    d.B, d.Hq, d.Hkv, d.Nq, d.Nk, d.D = 1, 4, 4, 640, 640, D
     for dst, t in ((d.q_stride, q), (d.k_stride, k), (d.v_stride, v), (d.o_stride, out)):
         dst[0], dst[1], dst[2] = t.stride(0), t.stride(1), t.stride(2)
     d.q, d.k, d.v, d.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
@@ -313,6 +314,41 @@ def test_dense_causal_mask_equals_causal_variant(pkg, wl):
     assert rc == 0, pkg.last_error()
     pkg.check_status(0)
     assert torch.equal(out, a)
+
+
+def test_d64_block_sparse_mask_many_pairs_per_cta(pkg, wl, oracle):
+    """d = 64 runs the S GEMM of the next KV tile as soon as the softmax has
+    read S (P in TMEM columns of its own).  Per-slice block-sparse masks over
+    640 work items (several per persistent CTA), so the two Q tiles of a pair
+    skip different KV tiles and the per-tile barrier phases carry across
+    pairs; a sample of slices is checked against the oracle."""
+    B, H, N, D = 4, 40, 1024, 64
+    w = wl.Workload("t", "bf16", B, H, H, N, D, False, seed=77)
+    inp = wl.make_inputs(w)
+    rng = np.random.default_rng(77)
+    nt = N // 128
+    kind = rng.choice(3, size=(B, H, nt, nt), p=[0.4, 0.35, 0.25])  # full, empty, mixed
+    kind[..., 0] = np.where(kind[..., 0] == 1, 0, kind[..., 0])
+    kind[1, 7, 3, 0] = 1                      # a Q tile whose first KV tile is masked: NaN rows
+    M = np.repeat(np.repeat(kind == 1, 128, axis=-2), 128, axis=-1)
+    mixed = np.repeat(np.repeat(kind == 2, 128, axis=-2), 128, axis=-1)
+    M |= mixed & (rng.integers(0, 5, size=(B, H, N, N), dtype=np.uint8) < 2)
+    q, k, v = wl.to_device(inp, w)
+    L = torch.empty((B, H, N), dtype=torch.float32, device="cuda")
+    out = pkg.fused(q, k, v, w.scale, mask=torch.from_numpy(M).cuda(), lse=L)
+    pkg.check_status(0)
+    slices = [0, 1 * H + 7, 63, 101, 2 * H + 39, B * H - 1]
+    ref, ref_lse = oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale, mask=M, slices=slices)
+    got = out.float().cpu().numpy().reshape(B * H, N, D)[slices]
+    lse = L.cpu().numpy().reshape(B * H, N)[slices]
+    ref = ref.reshape(B * H, N, D)[slices]
+    ref_lse = ref_lse.reshape(B * H, N)[slices]
+    nan_rows = np.isnan(ref).all(axis=-1)
+    assert nan_rows[1, 384:512].all()
+    assert (np.isnan(got) == np.isnan(ref)).all()
+    assert (np.isnan(lse) == np.isnan(ref_lse)).all()
+    assert _rel(got[~nan_rows], ref[~nan_rows]) <= 2e-2
+    assert np.abs(lse[~nan_rows] - ref_lse[~nan_rows]).max() <= 1e-3
 
 
 def test_bf16_mask_memref_with_host_buffers(pkg, wl, oracle):
