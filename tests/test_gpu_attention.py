@@ -727,3 +727,73 @@ def test_negative_and_zero_scale(pkg, oracle, scale, kind):
                                            M.cpu().numpy(), (B, H, N, N)))
     assert _rel(out.float().cpu().numpy(), ref) <= 2e-2
     assert np.abs(L.cpu().numpy() - ref_lse).max() <= 1e-3
+
+
+def test_concurrent_streams_match_serial(pkg, wl):
+    """Calls on two streams at once (causal and dense-mask calls on one, a
+    no-mask call on the other; the dense call's scratch is stream-ordered)
+    give the same bits as the same calls run one after another."""
+    w = wl.Workload("t", "bf16", 2, 8, 8, 2048, 128, True, seed=91)
+    inp = wl.make_inputs(w)
+    q, k, v = wl.to_device(inp, w)
+    q2, k2, v2 = (t.flip(2).contiguous() for t in (q, k, v))
+    m = torch.rand(2048, 2048, device="cuda") < 0.3
+    ref1 = pkg.fused(q, k, v, w.scale, causal=True)
+    ref2 = pkg.fused(q2, k2, v2, w.scale)
+    ref3 = pkg.fused(q2, k, v2, w.scale, mask=m, classify=False)
+    torch.cuda.synchronize()
+    pkg.check_status(0)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    outs = []
+    for _ in range(4):
+        with torch.cuda.stream(s1):
+            a = pkg.fused(q, k, v, w.scale, causal=True)
+            c = pkg.fused(q2, k, v2, w.scale, mask=m, classify=False)
+        with torch.cuda.stream(s2):
+            b = pkg.fused(q2, k2, v2, w.scale)
+        outs.append((a, b, c))
+    torch.cuda.synchronize()
+    pkg.check_status(0)
+    for a, b, c in outs:
+        assert torch.equal(a, ref1) and torch.equal(b, ref2) and torch.equal(c, ref3)
+
+
+def test_cuda_graph_capture_replays(pkg, wl):
+    """One causal call and one dense-mask call (classifier, ordering kernel,
+    stream-ordered scratch, attention kernel) captured into a CUDA graph:
+    replays on new inputs copied into the captured buffers give the same bits
+    as eager calls on those inputs."""
+    w = wl.Workload("t", "bf16", 1, 8, 8, 1024, 128, True, seed=93)
+    inp = wl.make_inputs(w)
+    q, k, v = wl.to_device(inp, w)
+    m = torch.rand(1024, 1024, device="cuda") < 0.25
+    o1, o2 = torch.empty_like(q), torch.empty_like(q)
+    L = torch.empty((1, 8, 1024), dtype=torch.float32, device="cuda")
+
+    def calls():
+        pkg.fused(q, k, v, w.scale, output=o1, causal=True, lse=L)
+        pkg.fused(q, k, v, w.scale, mask=m, output=o2, classify=False)
+
+    calls()  # first-call setup (kernel attributes, device state) outside capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            calls()
+    torch.cuda.synchronize()
+    for seed in (1, 2):
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(seed)
+        for t in (q, k, v):
+            t.copy_(torch.randn(t.shape, generator=gen, device="cuda").to(t.dtype))
+        g.replay()
+        torch.cuda.synchronize()
+        pkg.check_status(0)
+        L_e = torch.empty_like(L)
+        e1 = pkg.fused(q, k, v, w.scale, causal=True, lse=L_e)
+        e2 = pkg.fused(q, k, v, w.scale, mask=m, classify=False)
+        torch.cuda.synchronize()
+        assert torch.equal(o1, e1) and torch.equal(L, L_e) and torch.equal(o2, e2)
+    del g
