@@ -344,14 +344,15 @@ def main():
         clocks.start()
     n0 = pkg.launch_count()
     if rank_bytes(w, args) > L2_BYTES:
-        # Operands larger than L2: back-to-back steps between two events.
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record(stream)
-        for _ in range(args.steps):
+        # Operands larger than L2: back-to-back steps, an event between steps.
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        evs[0].record(stream)
+        for i in range(args.steps):
             step()
-        ev1.record(stream)
+            evs[i + 1].record(stream)
         torch.cuda.synchronize(dev)
-        ms = ev0.elapsed_time(ev1)
+        ms = evs[0].elapsed_time(evs[-1])
+        step_ms = [a.elapsed_time(b) for a, b in zip(evs[:-1], evs[1:])]
     else:
         # Operands fit in L2: write a 256 MB buffer before every step, outside
         # that step's pair of events, so no step starts with a warm L2.  A
@@ -368,7 +369,8 @@ def main():
             step()
             b.record(stream)
         torch.cuda.synchronize(dev)
-        ms = sum(a.elapsed_time(b) for a, b in evs)
+        step_ms = [a.elapsed_time(b) for a, b in evs]
+        ms = sum(step_ms)
         del flush
     launches = pkg.launch_count() - n0
     clk = clocks.stop() if clocks else None
@@ -395,7 +397,7 @@ def main():
         validation = validate_gathered(w, q, k, v, out, rank, world, qd, kd, vd)
 
     if rank == 0:
-        emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validation)
+        emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validation, step_ms)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -486,7 +488,20 @@ def run_e2e(args, pkg, w, q, k, v, out, descales, B, Hq, job_flops, world, dev, 
             "path": "_mlir_ciface_attn_fused_*_4d with pinned host memrefs"}
 
 
-def emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validation=None):
+def step_stats(step_ms):
+    """Median and spread of rank 0's per-step device times; steps that vary
+    by more than 5 % (relative standard deviation) are flagged."""
+    if not step_ms:
+        return None
+    med = statistics.median(step_ms)
+    std = statistics.pstdev(step_ms)
+    return {"median_ms": med, "std_ms": std, "min_ms": min(step_ms), "max_ms": max(step_ms),
+            "rel_std": std / med if med > 0 else 0.0,
+            "over_5pct": bool(med > 0 and std / med > 0.05)}
+
+
+def emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validation=None,
+         step_ms=None):
     peaks, peak_src = load_peaks()
     kernel_ms = ms / args.steps  # one launch per step on this rank
     achieved = w.flops(slices) / (kernel_ms * 1e-3) / 1e12
@@ -513,6 +528,7 @@ def emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validat
         "e2e": e2e,
         "gpu_launches": launches,
         "clocks": clk,
+        "step_times": step_stats(step_ms),
     }
     if validation is not None:
         line["validation"] = validation
