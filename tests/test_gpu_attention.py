@@ -388,13 +388,15 @@ def test_bounded_wait_times_out_and_device_stays_usable(pkg, wl, oracle):
     assert _rel(got, ref) <= 2e-2
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("Nq,Nk,causal", [(300, 700, False), (300, 700, True), (700, 300, True),
                                           (128, 1024, False), (1000, 129, False)])
-def test_unequal_query_and_key_lengths(pkg, wl, oracle, Nq, Nk, causal):
+def test_unequal_query_and_key_lengths(pkg, wl, oracle, Nq, Nk, causal, D):
     """Cross-attention shapes (Nq != Nk), ragged tiles on both sides; causal
-    is the op's mask[i][j] = j > i (top-left aligned)."""
+    is the op's mask[i][j] = j > i (top-left aligned).  d = 64 runs the early-S
+    schedule, d = 128 the S-behind-P·V one."""
     rng = np.random.Generator(np.random.PCG64(Nq * 7 + Nk))
-    B, H, D = 2, 2, 128
+    B, H = 2, 2
     qf = wl.round_bf16(rng.standard_normal((B, H, Nq, D), dtype=np.float32))
     kf = wl.round_bf16(rng.standard_normal((B, H, Nk, D), dtype=np.float32))
     vf = wl.round_bf16(rng.standard_normal((B, H, Nk, D), dtype=np.float32))
@@ -704,14 +706,15 @@ def test_input_output_type_matrix(pkg, oracle, in_dt, out_dt):
     assert _rel(out.float().cpu().numpy(), ref) <= 2e-2
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("scale", [-0.09, 0.0])
 @pytest.mark.parametrize("kind", ["causal", "dense"])
-def test_negative_and_zero_scale(pkg, oracle, scale, kind):
+def test_negative_and_zero_scale(pkg, oracle, scale, kind, D):
     """The op's scale is any f32: a negative scale flips which score is the
     row maximum (the kernel reduces with min then), zero gives uniform weights
     over the visible keys."""
     g = torch.Generator(device="cuda").manual_seed(50)
-    B, H, N, D = 1, 2, 400, 128
+    B, H, N = 1, 2, 400
     q, k, v = (torch.randn((B, H, N, D), generator=g, device="cuda").to(torch.bfloat16)
                for _ in range(3))
     M = None
