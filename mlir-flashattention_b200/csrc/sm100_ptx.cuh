@@ -53,11 +53,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// A thread whose phase is not complete is suspended for up to 2 us (or
+// until the phase completes) before the call returns false.  Without the
+// hint the suspension is shorter and waiting warps poll more often, taking
+// issue slots from the softmax warps that share their SM sub-partition: the
+// hint is worth +2 % on c4 in the power-capped steady state.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 2000;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
