@@ -293,10 +293,13 @@ def main():
         import datetime  # noqa: PLC0415
         # Keep rank 0's stdout to the one JSON line: NCCL writes its log,
         # including the version banner it prints at the WARN and VERSION
-        # levels, to stdout unless NCCL_DEBUG_FILE names another file.
+        # levels, to stdout unless NCCL_DEBUG_FILE names another file.  The
+        # file is a per-process one under /tmp: naming /dev/stderr makes NCCL
+        # reopen (and truncate) the stream's target when stderr is a regular
+        # file, which overwrote the start of a shared stdout/stderr log.
         if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
             os.environ["NCCL_DEBUG"] = "WARN"
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/tmp/attn_bench_nccl.%h.%p.log")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
