@@ -22,9 +22,18 @@ Keys beyond the base contract:
   e2e           the same metric through the C ABI memref entry with pinned
                 HOST buffers (host->device copies of Q/K/V and device->host
                 copies of O/LSE inside the timed region).
-  clocks        SM clock and throttle reasons sampled (NVML) during the timed
-                region.
-`--impl reference` times the oracle on the host cores instead (rank 0 only).
+  clocks        SM clock (median, min, share more than 100 MHz below max)
+                and throttle reasons sampled (NVML) during the timed region.
+  step_times    median / std / min / max of rank 0's per-step device times
+                and a flag when their relative std exceeds 5 %.
+
+Steps: without --steps, workloads whose operands exceed L2 run back to back
+for about 1.5 s (count from a short probe, MAX over ranks): the power-capped
+steady state, compared with the sustained peak.  L2-flushed workloads run 50
+separate steps against the burst peak.  With --steps K the peak is chosen by
+the timed region's length (sustained above 1 s).
+`--impl reference` times the oracle on the host cores instead (rank 0 only;
+50 steps without --steps).
 """
 from __future__ import annotations
 
