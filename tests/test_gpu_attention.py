@@ -390,7 +390,8 @@ def test_bounded_wait_times_out_and_device_stays_usable(pkg, wl, oracle):
 
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("Nq,Nk,causal", [(300, 700, False), (300, 700, True), (700, 300, True),
-                                          (128, 1024, False), (1000, 129, False)])
+                                          (128, 1024, False), (1000, 129, False), (300, 5, False),
+                                          (5, 300, True)])
 def test_unequal_query_and_key_lengths(pkg, wl, oracle, Nq, Nk, causal, D):
     """Cross-attention shapes (Nq != Nk), ragged tiles on both sides; causal
     is the op's mask[i][j] = j > i (top-left aligned).  d = 64 runs the early-S
