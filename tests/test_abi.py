@@ -107,3 +107,48 @@ def test_device_memory_helpers_without_a_gpu(pkg):
     assert L.attn_rt_copy(None, ctypes.byref(p), 8, None) == -1
     if not torch.cuda.is_available():
         assert L.attn_rt_alloc(ctypes.byref(p), 256) == -9
+
+
+def _pass_callees():
+    """(callee, argument count) for every call the --attention-to-runtime
+    pass can emit, following its rules (mlir/RuntimeLoweringPass.cpp): f32
+    lowers in rank 2 or 4, the other types in rank 4; a general i1 mask only
+    for rank-2 f32 and rank-4 bf16; arguments Q, K, V, scale, three descales
+    for e4m3, the mask, O, and an LSE memref for the non-f32 entries."""
+    src = open(os.path.join(ROOT, "mlir-flashattention_b200", "mlir",
+                            "RuntimeLoweringPass.cpp")).read()
+    assert 'std::string callee = ("attn_fused_" + dt + "_").str();' in src
+    assert '(dt == "f32" && rank == 2) || (dt == "bf16" && rank == 4)' in src
+    out = []
+    for dt in ("f32", "bf16", "f16", "e4m3"):
+        for rank in (2, 4):
+            if dt != "f32" and rank != 4:
+                continue
+            for kind in ("nomask", "causal", "mask"):
+                if kind == "mask" and not ((dt == "f32" and rank == 2) or (dt == "bf16" and rank == 4)):
+                    continue
+                name = f"attn_fused_{dt}_{kind}" + ("_4d" if rank == 4 else "")
+                nargs = 4 + (3 if dt == "e4m3" else 0) + (1 if kind == "mask" else 0) + 1 + \
+                    (1 if dt != "f32" else 0)
+                out.append((name, nargs))
+    return out
+
+
+def test_every_call_the_lowering_pass_emits_is_declared_with_its_arity():
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    protos = {m.group(1): m.group(2) for m in
+              re.finditer(r"_mlir_ciface_(\w+)\s*\(([^;{]*)\)\s*;", text)}
+    callees = _pass_callees()
+    assert len(callees) == 12
+    for name, nargs in callees:
+        assert name in protos, name
+        assert protos[name].count(",") + 1 == nargs, (name, protos[name])
+
+
+def test_every_call_the_lowering_pass_emits_is_exported(pkg):
+    pkg.lib()
+    out = subprocess.run(["nm", "-D", "--defined-only", pkg.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if ln.strip()}
+    missing = ["_mlir_ciface_" + n for n, _ in _pass_callees() if "_mlir_ciface_" + n not in exported]
+    assert not missing, missing
