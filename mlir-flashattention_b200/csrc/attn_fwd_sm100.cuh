@@ -16,8 +16,9 @@
 //               S_t = Q_t·K_jᵀ into TMEM (SS form), O_t += P_t·V_j with P_t
 //               read from TMEM (TS form); order per KV step
 //               P·V_0(j), S_0(j'), P·V_1(j), S_1(j') where j' is the next
-//               KV tile of the pair's list (PairSched); each S GEMM follows
-//               the P·V GEMM reading the same TMEM columns in issue order.
+//               KV tile of the pair's list (PairSched); each S GEMM is
+//               issued once the P·V GEMM reading P from its TMEM columns has
+//               completed (gate_S).
 //               d = 64 ("early S", P in columns of its own): S_0(j'), S_1(j')
 //               as soon as each softmax has read its S, then P·V_0(j),
 //               P·V_1(j).
@@ -583,6 +584,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           auto kph = [&](int i) { return (ring + 2 * i) / C::kStages; };
           auto vst = [&](int i) { return (ring + 2 * i + 1) % C::kStages; };
           auto vph = [&](int i) { return (ring + 2 * i + 1) / C::kStages; };
+          // S_t's columns hold P_t, which the last P·V GEMM of tile t reads.
+          // The PTX ISA orders two tcgen05.mma operations of one thread only
+          // when they share cta_group, accumulator and shape (its pipelined
+          // instruction pairs); the S GEMM (accumulator S_t, N = 128) and the
+          // P·V GEMM (accumulator O_t, N = D) are not such a pair, so the S
+          // GEMM is issued only once the P·V GEMM has completed (its commit
+          // on pv_done[t]).  This also makes "S_t(j+1) complete" imply
+          // "P·V_t(j) complete" for the softmax, which rewrites P_t and
+          // rescales O_t after it sees S_t(j+1).
+          auto gate_S = [&](int t) {
+            if (pv_cnt[t] > 0 && !wait(&pv_done[t], pv_cnt[t] - 1)) return false;
+            tc_fence_after();
+            return true;
+          };
           if (!wait(q_full, qi) || !wait(&kv_full[kst(0)], kph(0))) {
             ok = false;
             break;
@@ -590,9 +605,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           for (int t = 0; t < 2 && ok; ++t) {
             if (!sc.act(t, kt0)) continue;
-            // S_t's columns may still hold the previous pair's last P_t, read by
-            // a P·V GEMM issued earlier from this thread (see the ordering note
-            // below).
+            // The previous pair's last P·V GEMM of this tile may still read P_t.
+            if (!gate_S(t)) {
+              ok = false;
+              break;
+            }
             issue_S(t, kst(0));
             mma_commit_lead(lead, &s_full[t]);
           }
@@ -600,15 +617,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit_lead(lead, &kv_empty[kst(0)]);  // K free once its S GEMMs finish
           if (sc.next(kt0) >= kt_end) mma_commit_lead(lead, q_empty);  // all S GEMMs issued
           // Per KV tile, for each Q tile t that needs it: O_t += P_t·V, then
-          // S_t = Q_t·Kᵀ of t's next KV tile right behind it.  P_t lives in the
-          // S_t columns; the S GEMM is issued without waiting for the P·V GEMM
-          // to complete because tcgen05.mma operations issued by one thread run
-          // through the tensor pipe in issue order, so the S GEMM's accumulator
-          // writes come after the P·V GEMM's reads of P_t.  (CUTLASS's SM100
-          // attention mainloop issues its S GEMM behind the P·V GEMM on the
-          // same columns the same way.  Waiting for P·V completion instead
-          // costs a pipe drain per tile step: 2-7 % measured, identical bits.)
-          // Tile t's next softmax then overlaps the other tile's GEMMs.
+          // S_t = Q_t·Kᵀ of t's next KV tile once that P·V GEMM has completed
+          // (gate_S: P_t lives in the S_t columns).  Tile t's next softmax
+          // then overlaps the other tile's GEMMs.
           bool first_pv[2] = {true, true};
           int kn_ahead = DENSE ? sc.next(kt0) : 0;
           for (int kt = kt0; kt < kt_end && ok; ++i) {
@@ -654,11 +665,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               mma_commit_lead(lead, &pv_done[t]);
               ++pv_cnt[t];
               if (DENSE ? act_kn[t] : (kn < kt_end && sc.act(t, kn))) {
-                if (!wait_k_next()) {
+                if (!wait_k_next() || !gate_S(t)) {
                   ok = false;
                   break;
                 }
-                tc_fence_after();
                 issue_S(t, kst(i + 1));
                 mma_commit_lead(lead, &s_full[t]);
               }
@@ -668,11 +678,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               // A Q tile that skipped kt but needs kn gets its S GEMM here.
               for (int t = 0; t < 2 && ok; ++t) {
                 if (act_kt[t] || !act_kn[t]) continue;
-                if (!wait_k_next()) {
+                if (!wait_k_next() || !gate_S(t)) {
                   ok = false;
                   break;
                 }
-                tc_fence_after();
                 issue_S(t, kst(i + 1));
                 mma_commit_lead(lead, &s_full[t]);
               }
@@ -881,7 +890,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             // P_t's columns and O_t: the previous P·V GEMM of this tile reads
             // the one and accumulates into the other, so it must be complete
             // before P_t is rewritten or O_t rescaled.  (Without early S the
-            // completion of this S GEMM, issued behind it, implies it.)
+            // MMA warp issues this S GEMM only after that P·V GEMM completed,
+            // so the completion of the S GEMM implies it.)
             if (steps > 0 && !warp_wait(&pv_done[t], static_cast<uint32_t>((steps - 1) & 1),
                                         abort_flag, p.status)) {
               ok = false;

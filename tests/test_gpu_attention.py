@@ -149,25 +149,6 @@ def test_e4m3_block_descales(pkg, wl, oracle, causal, nq, nk):
         pkg.fused(bf, bf, bf, 0.1, q_descale=torch.ones((1, 1, 1), device="cuda"))
 
 
-def test_c4_sampled_rows(pkg, wl, oracle):
-    """Full c4 size (bf16 causal B=1 H=32 N=16384 D=128): every output finite,
-    sampled Q tiles of the first and last head against the oracle."""
-    w = wl.WORKLOADS["c4"]
-    inp = wl.make_inputs(w)
-    got, lse = _run_pkg(pkg, wl, w, inp, True)
-    assert np.isfinite(got).all() and np.isfinite(lse).all()
-    ref = np.zeros_like(inp.qf)
-    ref_lse = np.zeros(inp.qf.shape[:3], np.float32)
-    oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale, causal=True, slices=[0, 31],
-                        tile_offset=3, tile_stride=16, out=ref, lse_out=ref_lse)
-    for h in (0, 31):
-        for t in range(3, 128, 16):
-            rows = slice(t * 128, t * 128 + 128)
-            g, r = got[0, h, rows], ref[0, h, rows]
-            assert _rel(g, r) <= w.tol, (h, t)
-            assert np.abs(lse[0, h, rows] - ref_lse[0, h, rows]).max() <= 1e-3
-
-
 def test_strided_operands_match_contiguous(pkg, wl):
     """A [B, N, H, D] buffer viewed as [B, H, N, D] (non-contiguous heads)."""
     w = wl.Workload("t", "bf16", 2, 4, 4, 256, 128, True, seed=5)
