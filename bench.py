@@ -7,9 +7,11 @@ A step is one `attention.fused` call over the workload's (batch, head)
 slices.  Default workload: bf16 causal attention B=1, H=32, N=16384, d=128
 (scale 1/sqrt(128)), inputs N(0,1) drawn from a seeded generator.  With N GPUs
 (one process per GPU, torchrun) each rank owns an independent shard of
-slices; there is no collective in the timed region.  Weak scaling (default):
-every rank runs the full per-GPU workload, so the global batch is N x B.
-Strong scaling: the workload's slices are split across ranks.
+slices; there is no collective in the timed region.  Strong scaling (default,
+as the workload is stated: its 32 heads sharded over the GPUs, 4 per GPU at
+N = 8): the workload's (batch, kv-head) groups are split across ranks in
+contiguous blocks.  Weak scaling (--scaling weak): every rank runs the full
+workload, so the global batch is N x B.
 
 Metric: causal-adjusted attention TFLOP/s (4·N²·d per slice, halved when
 causal), whole job = all ranks' FLOPs / max-over-ranks device time.
@@ -138,7 +140,7 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_sample(w, budget_s=12.0, max_tiles=None):
+def cpu_sample(w, budget_s=12.0, max_tiles=None, threads=None):
     """Time the oracle on c. `budget_s` of q tiles of the workload (all host
     threads; one tile per thread per batch) and extrapolate to the workload.
 
@@ -150,7 +152,7 @@ def cpu_sample(w, budget_s=12.0, max_tiles=None):
     import __graft_entry__ as ge  # noqa: PLC0415
 
     o = ge.oracle()
-    cores = host_threads()
+    cores = threads or host_threads()
     rng = np.random.Generator(np.random.PCG64(w.seed))
     # One (batch, head) slice of the workload's shape is enough: every slice
     # costs the same.
@@ -188,7 +190,7 @@ def reference_arm(args, w, world):
     import __graft_entry__ as ge  # noqa: PLC0415
 
     o = ge.oracle()
-    cores = host_threads()
+    cores = args.threads or host_threads()
     rng = np.random.Generator(np.random.PCG64(w.seed))
     q = rng.standard_normal((1, 1, w.N, w.D), dtype=np.float32)
     k = rng.standard_normal((1, 1, w.N, w.D), dtype=np.float32)
@@ -235,6 +237,23 @@ def reference_arm(args, w, world):
 L2_BYTES = 126e6  # B200 L2
 
 
+def echo_nccl_log():
+    """Copy this process's NCCL log lines (NCCL_DEBUG_FILE, %h = host name,
+    %p = pid) to stderr."""
+    import socket  # noqa: PLC0415
+
+    path = os.environ.get("NCCL_DEBUG_FILE", "")
+    path = path.replace("%h", socket.gethostname()).replace("%p", str(os.getpid()))
+    try:
+        with open(path) as f:
+            lines = f.read().splitlines()
+    except OSError:
+        return
+    for ln in lines:
+        if "NCCL" in ln:
+            print(ln, file=sys.stderr, flush=True)
+
+
 def rank_bytes(w, args):
     """Algorithmic bytes of one rank's shard (Q, K, V, O, LSE)."""
     return w.bytes() * getattr(args, "rank_slices", w.B * w.Hq) / (w.B * w.Hq)
@@ -245,7 +264,10 @@ def config_dict(w, world, args):
     return {
         "workload": w.name, "global_batch": per_rank_b * world if args.scaling == "weak" else w.B,
         "heads_q": w.Hq, "heads_kv": w.Hkv, "seq_len": w.N, "head_dim": w.D,
-        "causal": w.causal, "scale": w.scale, "parallelism": f"slice-shard x{world}",
+        "causal": w.causal, "scale": w.scale,
+        "parallelism": (f"slice-shard x{world}: (batch, kv-head) groups split over ranks"
+                        if args.scaling == "strong" else
+                        f"slice-shard x{world}: every rank runs the whole workload"),
         "l2": "per-GPU operands larger than L2 (> 126 MB); no flush"
         if rank_bytes(w, args) > L2_BYTES else "L2 flushed (256 MB write) before every timed step",
         **({"mask": "causal pattern as an explicit i1 mask, broadcast, dense-mask kernel"}
@@ -262,15 +284,22 @@ def main():
                          "compared with the sustained peak; L2-flushed workloads run 50)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="c4")
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="strong")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--threads", type=int, default=None,
+                    help="host threads for the oracle legs (cpu_baseline and --impl "
+                         "reference); default: every core this process may use")
     ap.add_argument("--validate", action="store_true",
                     help="after timing, gather each rank's first slice (Q, K, V, sampled O "
                          "tiles) to rank 0 over the process group and check it against the oracle")
     ap.add_argument("--heads", type=int, default=None,
                     help="override the query-head count (reduced profiling case)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the batch size (profiling case)")
+    ap.add_argument("--seq", type=int, default=None,
+                    help="override the sequence length (profiling case)")
     ap.add_argument("--dense-mask", action="store_true",
                     help="causal workloads: pass the causal pattern as an explicit i1 mask "
                          "(broadcast) and run the dense-mask kernel")
@@ -287,6 +316,10 @@ def main():
         import dataclasses  # noqa: PLC0415
         w = dataclasses.replace(w, name=f"{w.name}_h{args.heads}", Hq=args.heads,
                                 Hkv=max(1, args.heads * w.Hkv // w.Hq))
+    if args.batch or args.seq:
+        import dataclasses  # noqa: PLC0415
+        B, N = args.batch or w.B, args.seq or w.N
+        w = dataclasses.replace(w, name=f"{w.name}_b{B}n{N}", B=B, N=N)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         return reference_arm(args, w, world)
@@ -306,11 +339,18 @@ def main():
         # file is a per-process one under /tmp: naming /dev/stderr makes NCCL
         # reopen (and truncate) the stream's target when stderr is a regular
         # file, which overwrote the start of a shared stdout/stderr log.
-        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-            os.environ["NCCL_DEBUG"] = "WARN"
+        # INIT-level lines (communicator size and rank) go to that file and
+        # are copied to stderr once the communicator exists, so a reader of
+        # the run's stderr can check every rank joined an N-rank
+        # communicator.
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION", "WARN"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         os.environ.setdefault("NCCL_DEBUG_FILE", "/tmp/attn_bench_nccl.%h.%p.log")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
+        dist.barrier()
+        echo_nccl_log()
 
     # This rank's shard of (batch, head) slices.
     if args.scaling == "weak":
@@ -582,7 +622,7 @@ def emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validat
     if validation is not None:
         line["validation"] = validation
     if world == 1 and not args.no_cpu_baseline:
-        tf, cores, text = cpu_sample(w)
+        tf, cores, text = cpu_sample(w, threads=args.threads)
         line["cpu_baseline"] = {"value": tf, "unit": "TFLOP/s", "cores": cores,
                                 "kind": "port", "sample": text}
     print(json.dumps(line), flush=True)

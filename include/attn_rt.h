@@ -117,6 +117,16 @@ ATTN_API int attn_fwd(const AttnDesc* desc, void* stream);
  * per-device status word.  Called implicitly by attn_fwd. */
 ATTN_API int attn_rt_init(int device);
 
+/* Schedule of causal tensor-core calls (no counterpart in the reference).
+ * A causal launch with few Q-tile pairs per SM is bounded by its heaviest
+ * pairs; the runtime then runs the S heaviest pair indices of every slice as
+ * two work items over the first and second half of their KV tiles and merges
+ * the halves in the kernel (stream-ordered scratch: 128 x (D + 1) floats per
+ * Q tile and half).  Returns the S a causal call with `slices` (batch x
+ * q-head) slices of Nq x Nk would use on a device with `sm_count` SMs
+ * (0: no split).  attn_fwd_host_noalloc never splits. */
+ATTN_API int attn_rt_causal_split(int64_t slices, int64_t Nq, int64_t Nk, int sm_count);
+
 /* Synchronise `stream`, read and clear the device status word written by the
  * kernels of `device`; returns ATTN_OK or the first recorded ATTN_ERR_*. */
 ATTN_API int attn_rt_check_status(int device, void* stream);
@@ -211,6 +221,14 @@ ATTN_API int32_t _mlir_ciface_attn_fused_bf16_mask_4d(AttnMemRef4D* Q, AttnMemRe
                                                       AttnMemRef4D* mask, AttnMemRef4D* O,
                                                       AttnMemRef4D* LSE);
 
+/* Rank-4 bf16 operands with the op's own rank-2 i1 mask memref<NqxNkxi1>
+ * (AttentionOps.td:26-28,40), applied to every (batch, head) slice.  The
+ * lowering pass calls this entry when a rank-2 mask meets rank-4 operands. */
+ATTN_API int32_t _mlir_ciface_attn_fused_bf16_mask2d_4d(AttnMemRef4D* Q, AttnMemRef4D* K,
+                                                        AttnMemRef4D* V, float scale,
+                                                        AttnMemRef2D* mask, AttnMemRef4D* O,
+                                                        AttnMemRef4D* LSE);
+
 /* Rank-4 e4m3 in (per-tensor dequantisation factors) / bf16 out. */
 ATTN_API int32_t _mlir_ciface_attn_fused_e4m3_nomask_4d(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V,
                                                float scale, float q_descale, float k_descale,
@@ -239,10 +257,17 @@ ATTN_API int32_t _mlir_ciface_attn_fused_e4m3_causal_4d(AttnMemRef4D* Q, AttnMem
  * ATTN_NOALLOC_SCRATCH_BYTES - 256 bytes is rejected with ATTN_ERR_SHAPE and
  * a message giving both sizes.
  *
+ * Host buffers may have any alignment and row strides (each chunk is
+ * re-packed into aligned staging regions); device pointers are refused with
+ * ATTN_ERR_INVALID (device-resident operands go to attn_fwd).
+ *
  * The first call on each device resolves the array's device address
  * (cudaGetSymbolAddress, with that device current); make that first call
- * before any stream capture.  Copies and kernels run on `stream` and the call
- * returns after O (and LSE) are back in host memory.  All calls share the one
+ * before any stream capture.  A set-up that fails is not remembered, so a
+ * later call retries it.  Copies and kernels run on `stream` and the call
+ * returns after O (and LSE) are back in host memory; an error after the
+ * first copy was enqueued also waits for `stream` before returning, so the
+ * caller may reuse its buffers whatever the outcome.  All calls share the one
  * array, which keeps the previous call's contents (the status word is
  * cleared at the start of each call): calls that overlap on the GPU — from
  * several threads or streams of one process — race and must be serialised by

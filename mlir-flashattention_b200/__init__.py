@@ -95,6 +95,9 @@ def lib():
         L.attn_fwd.argtypes = [ctypes.POINTER(AttnDesc), ctypes.c_void_p]
         L.attn_rt_init.restype = ctypes.c_int
         L.attn_rt_init.argtypes = [ctypes.c_int]
+        L.attn_rt_causal_split.restype = ctypes.c_int
+        L.attn_rt_causal_split.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_int]
         L.attn_rt_check_status.restype = ctypes.c_int
         L.attn_rt_check_status.argtypes = [ctypes.c_int, ctypes.c_void_p]
         L.attn_rt_status_string.restype = ctypes.c_char_p
@@ -127,6 +130,8 @@ def lib():
             fn.restype, fn.argtypes = ctypes.c_int32, [m4, m4, m4, f, f, f, f, m4, m4]
         L._mlir_ciface_attn_fused_bf16_mask_4d.restype = ctypes.c_int32
         L._mlir_ciface_attn_fused_bf16_mask_4d.argtypes = [m4, m4, m4, f, m4, m4, m4]
+        L._mlir_ciface_attn_fused_bf16_mask2d_4d.restype = ctypes.c_int32
+        L._mlir_ciface_attn_fused_bf16_mask2d_4d.argtypes = [m4, m4, m4, f, m2, m4, m4]
         L._mlir_ciface_attn_fused_f32_mask.restype = ctypes.c_int32
         L._mlir_ciface_attn_fused_f32_mask.argtypes = [m2, m2, m2, f, m2, m2]
         _lib = L

@@ -91,6 +91,16 @@ struct FwdParams {
   // Dense mode: work items (slice-major index) ordered by decreasing number
   // of KV tiles visited (order_dense_items), for the persistent schedule.
   const int* order;
+  // Causal mode, KV split (split_pairs > 0): the split_pairs heaviest pair
+  // indices of every slice run as two work items each, over the first and
+  // the second half of the pair's KV tiles.  Each half writes its rows'
+  // normalised output and log2-domain LSE to part_o / part_lse; the warp
+  // that finishes second (counted in part_cnt, zeroed before the launch)
+  // merges both halves into O and the LSE.
+  int split_pairs;
+  float4* part_o;   // [split][half][t][D/4][128 rows]
+  float* part_lse;  // [split][half][t][128 rows]
+  int* part_cnt;    // [split][t][4 warps]
 };
 
 // Classes of a 128 x 128 block of a dense mask (rows < Nq, keys < Nk).
@@ -169,8 +179,15 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* 
 // The persistent CTAs take items in a snake: round r gives CTA c item
 // r·G + c (r even) or r·G + G-1-c (r odd), which balances the decreasing
 // causal weights across CTAs.
+//
+// Causal KV split (FwdParams::split_pairs = S > 0, chosen by the host when
+// there are too few pairs per SM for the snake to balance): the list starts
+// with the two halves of each of the S heaviest pair indices (pair
+// num_pairs-1-j, j < S: half 0 of every slice, then half 1 of every slice),
+// followed by the unsplit pairs, heaviest first.
 struct Item {
   int bh, pair;
+  int half;  // -1: the whole pair; 0 / 1: first / second half of its KV tiles
 };
 
 template <bool CAUSAL>
@@ -179,17 +196,32 @@ __device__ __forceinline__ int item_index(int round, int cta, int G, int W) {
   return w < W ? w : -1;
 }
 
-template <bool CAUSAL>
-__device__ __forceinline__ Item decode_item(int w, int num_bh, int num_pairs) {
+template <bool CAUSAL, bool SPLIT>
+__device__ __forceinline__ Item decode_item(int w, int num_bh, int num_pairs, int split) {
   Item it;
+  it.half = -1;
   if (CAUSAL) {
-    it.pair = num_pairs - 1 - w / num_bh;
-    it.bh = w % num_bh;
+    const int ns = SPLIT ? 2 * split * num_bh : 0;  // split halves come first
+    if (SPLIT && w < ns) {
+      const int j = w / (2 * num_bh), rem = w - j * 2 * num_bh;
+      it.pair = num_pairs - 1 - j;
+      it.half = rem / num_bh;
+      it.bh = rem - it.half * num_bh;
+    } else {
+      w -= ns;
+      it.pair = num_pairs - 1 - split - w / num_bh;
+      it.bh = w % num_bh;
+    }
   } else {
     it.bh = w / num_pairs;
     it.pair = w % num_pairs;
   }
   return it;
+}
+
+// Work items of one launch.
+__host__ __device__ __forceinline__ int work_items(int num_bh, int num_pairs, int split) {
+  return num_bh * (num_pairs + split);
 }
 
 // KV tiles (of 128 keys) each of the two Q tiles of `pair` needs.
@@ -217,32 +249,44 @@ __device__ __forceinline__ void kv_counts(int pair, int Nq, int Nk, int (&n_t)[2
 // of the reference design, Design.md:412-419, applied to an arbitrary mask);
 // a Q tile whose first KV tile is empty needs none: its rows are NaN, as in
 // the reference (see the softmax).
-template <int MODE>
+template <int MODE, bool SPLIT>
 struct PairSched {
-  int n_t[2];             // prefix lengths (no-mask, causal)
+  int n_t[2];             // no-mask, causal: tile t needs KV tiles [lo, n_t[t])
+  int lo;                 // first KV tile of this item (second half of a split pair: > 0)
+  bool merge[2];          // split pair whose tile t has KV tiles in both halves
   const uint8_t* cls[2];  // dense: the Q tiles' class rows (nullptr: no KV tile)
   int nkt;                // dense: KV tiles per row
 
   __device__ __forceinline__ bool act(int t, int kt) const {
     if constexpr (MODE == kMaskDense)
       return cls[t] != nullptr && __ldg(cls[t] + kt) != kTileEmpty;
+    else if constexpr (SPLIT)
+      return kt >= lo && kt < n_t[t];
     else
       return kt < n_t[t];
   }
   __device__ __forceinline__ bool any(int t) const {
     if constexpr (MODE == kMaskDense) return cls[t] != nullptr;
+    else if constexpr (SPLIT) return n_t[t] > lo;
     else return n_t[t] > 0;
+  }
+  // First KV tile Q tile t needs (any(t) must hold).
+  __device__ __forceinline__ int first_t(int t) const {
+    if constexpr (SPLIT) return lo;
+    else return 0;
   }
   __device__ __forceinline__ int end() const {
     if constexpr (MODE == kMaskDense) return nkt;
     else return max(n_t[0], n_t[1]);
   }
-  // Next KV tile of the union after kt (end() if none).
+  // Next KV tile of the union after kt (end() if none); next(-1) is the first.
   __device__ __forceinline__ int next(int kt) const {
     if constexpr (MODE == kMaskDense) {
       for (++kt; kt < nkt; ++kt)
         if (act(0, kt) || act(1, kt)) break;
       return kt;
+    } else if constexpr (SPLIT) {
+      return max(kt + 1, lo);
     } else {
       return kt + 1;
     }
@@ -263,9 +307,11 @@ struct PairSched {
   }
 };
 
-template <int MODE>
-__device__ __forceinline__ PairSched<MODE> make_sched(const Item& itm, const FwdParams& p) {
-  PairSched<MODE> sc;
+template <int MODE, bool SPLIT>
+__device__ __forceinline__ PairSched<MODE, SPLIT> make_sched(const Item& itm, const FwdParams& p) {
+  PairSched<MODE, SPLIT> sc;
+  sc.lo = 0;
+  sc.merge[0] = sc.merge[1] = false;
   if constexpr (MODE == kMaskDense) {
     const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq;
     sc.nkt = p.nkt;
@@ -281,6 +327,16 @@ __device__ __forceinline__ PairSched<MODE> make_sched(const Item& itm, const Fwd
     kv_counts<MODE == kMaskCausal>(itm.pair, p.Nq, p.Nk, sc.n_t);
     sc.cls[0] = sc.cls[1] = nullptr;
     sc.nkt = 0;
+    if (SPLIT && itm.half >= 0) {
+      // Halves [0, mid) and [mid, end) of the pair's KV tiles.
+      const int mid = (max(sc.n_t[0], sc.n_t[1]) + 1) / 2;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        sc.merge[t] = sc.n_t[t] > mid;
+        if (itm.half == 0) sc.n_t[t] = min(sc.n_t[t], mid);
+      }
+      sc.lo = itm.half == 0 ? 0 : mid;
+    }
   }
   return sc;
 }
@@ -309,12 +365,16 @@ __device__ __forceinline__ void load_mask_row(const uint8_t* mrow, int kbase, in
   }
 }
 
-template <int D, int MODE, int ELT>
+// SPLIT: the causal launch with a KV split of its heaviest pairs
+// (FwdParams::split_pairs > 0); a separate specialisation, so launches
+// without a split run no split logic.
+template <int D, int MODE, int ELT, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   constexpr bool CAUSAL = MODE == kMaskCausal;
+  static_assert(!SPLIT || CAUSAL, "the KV split is a causal-mode schedule");
   constexpr bool DENSE = MODE == kMaskDense;
   using C = FwdCfg<D, ELT>;
   constexpr bool FP8 = C::FP8;
@@ -341,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int G = static_cast<int>(gridDim.x);
   const int cta = static_cast<int>(blockIdx.x);
-  const int W = p.num_bh * p.num_pairs;
+  const int W = work_items(p.num_bh, p.num_pairs, SPLIT ? p.split_pairs : 0);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -385,9 +445,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int r = 0; ok; ++r) {
           const int w = item_index<CAUSAL>(r, cta, G, W);
           if (w < 0) break;
-          const Item itm = decode_item<CAUSAL>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs);
+          const Item itm = decode_item<CAUSAL, SPLIT>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs, p.split_pairs);
           const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq, hk = h / p.group;
-          const PairSched<MODE> sc = make_sched<MODE>(itm, p);
+          const PairSched<MODE, SPLIT> sc = make_sched<MODE, SPLIT>(itm, p);
           const int kt_end = sc.end();
           int kt = sc.next(-1);
           if (kt >= kt_end) continue;  // no KV tile at all (dense: every row NaN)
@@ -490,8 +550,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int r = 0; ok; ++r) {
         const int w = item_index<CAUSAL>(r, cta, G, W);
         if (w < 0) break;
-        const Item itm = decode_item<CAUSAL>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs);
-        const PairSched<MODE> sc = make_sched<MODE>(itm, p);
+        const Item itm = decode_item<CAUSAL, SPLIT>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs, p.split_pairs);
+        const PairSched<MODE, SPLIT> sc = make_sched<MODE, SPLIT>(itm, p);
         const int kt_end = sc.end();
         const int kt0 = sc.next(-1);
         if (kt0 >= kt_end) continue;  // no KV tile (the producer skips the pair too)
@@ -729,8 +789,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int rr = 0; ok; ++rr) {
       const int w = item_index<CAUSAL>(rr, cta, G, W);
       if (w < 0) break;
-      const Item itm = decode_item<CAUSAL>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs);
-      const PairSched<MODE> sc = make_sched<MODE>(itm, p);
+      const Item itm = decode_item<CAUSAL, SPLIT>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs, p.split_pairs);
+      const PairSched<MODE, SPLIT> sc = make_sched<MODE, SPLIT>(itm, p);
       const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq;
       const int qs = itm.pair * 256 + 128 * t;
       const int row = qs + r;
@@ -771,7 +831,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.vd_head) vd = __ldg(p.vd_head + bk);
         if (p.kd_blk) {
           kd_row = p.kd_blk + static_cast<int64_t>(bk) * p.nkb;
-          kd_cur = __ldg(kd_row);
+          kd_cur = __ldg(kd_row + sc.first_t(t));  // the factor of this tile's first KV block
         }
       }
       // Dense masks: the reference's loop (TilingPass.cpp:291-305) evaluates
@@ -782,7 +842,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (DENSE)
         mrow = p.mask + b * p.m_sb + h * p.m_sh + static_cast<int64_t>(min(row, p.Nq - 1)) * p.m_sn;
       bool first = true;
-      for (int kt = 0; kt < kt_end; ++steps) {
+      for (int kt = sc.first_t(t); kt < kt_end; ++steps) {
         const int kn = sc.next_t(t, kt);
         // Dense: mask bits only for partial blocks (full ones mask nothing).
         const bool sel = DENSE && !sc.full(t, kt);
@@ -941,6 +1001,78 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
+      if constexpr (SPLIT) {
+        if (sc.merge[t]) {
+          // Half of a split pair: this warp's 32 rows go to the partial
+          // buffers (normalised O, LSE in the log2 domain; a row with no
+          // visible key in this half has weight 0), and the warp that comes
+          // second merges both halves, always as half 0 + half 1 so the
+          // result does not depend on which finished last.
+          const int sidx = (p.num_pairs - 1 - itm.pair) * p.num_bh + itm.bh;
+          const int slot = (sidx * 2 + itm.half) * 2 + t;
+          const float inv = l > 0.f ? p.o_scale * vd / l : 0.f;
+          float4* mine = p.part_o + static_cast<int64_t>(slot) * (D / 4) * 128 + r;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+            if (c == D / 32 - 1) {
+              tc_fence_before();
+              mbar_arrive(&o_free[t]);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              mine[(c * 8 + i) * 128] = make_float4(
+                  __uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                  __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+          }
+          p.part_lse[slot * 128 + r] = l > 0.f ? m + __log2f(l) : -INFINITY;
+          __threadfence();
+          __syncwarp();
+          int old = 0;
+          if (lane == 0) old = atomicAdd(p.part_cnt + (sidx * 2 + t) * 4 + quarter, 1);
+          old = __shfl_sync(0xffffffffu, old, 0);
+          if (old == 0) continue;  // the other half is still running and will merge
+          __threadfence();
+          const int s0 = (sidx * 2) * 2 + t, s1 = (sidx * 2 + 1) * 2 + t;
+          const float la = __ldcg(p.part_lse + s0 * 128 + r);
+          const float lb = __ldcg(p.part_lse + s1 * 128 + r);
+          const float mx = fmaxf(la, lb);
+          const float ea = ex2(la - mx), eb = ex2(lb - mx);
+          const float sum = ea + eb, wa = ea / sum, wb = eb / sum;
+          if (row < p.Nq) {
+            const float4* h0 = p.part_o + static_cast<int64_t>(s0) * (D / 4) * 128 + r;
+            const float4* h1 = p.part_o + static_cast<int64_t>(s1) * (D / 4) * 128 + r;
+            auto mix = [&](int c4) {
+              const float4 x = __ldcg(h0 + c4 * 128), y = __ldcg(h1 + c4 * 128);
+              return make_float4(fmaf(wb, y.x, wa * x.x), fmaf(wb, y.y, wa * x.y),
+                                 fmaf(wb, y.z, wa * x.z), fmaf(wb, y.w, wa * x.w));
+            };
+            const int64_t obase = static_cast<int64_t>(b) * p.o_sb +
+                                  static_cast<int64_t>(h) * p.o_sh +
+                                  static_cast<int64_t>(row) * p.o_sn;
+            if (p.out_kind == 1) {
+              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + obase);
+#pragma unroll 4
+              for (int c4 = 0; c4 < D / 4; ++c4) dst[c4] = mix(c4);
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.o) + obase);
+              const bool f16 = p.out_kind == 2;
+              auto pk = [&](float x, float y) { return f16 ? pack_f16(x, y) : pack_bf16(x, y); };
+#pragma unroll 4
+              for (int c8 = 0; c8 < D / 8; ++c8) {
+                const float4 u = mix(2 * c8), v = mix(2 * c8 + 1);
+                dst[c8] = make_uint4(pk(u.x, u.y), pk(u.z, u.w), pk(v.x, v.y), pk(v.z, v.w));
+              }
+            }
+            if (p.lse)
+              p.lse[static_cast<int64_t>(itm.bh) * p.Nq + row] =
+                  (mx + __log2f(sum)) * 0.69314718055994531f;
+          }
+          continue;
+        }
+      }
       const float inv_l = nan_row ? __int_as_float(0x7fc00000) : p.o_scale * vd / l;
       const int64_t obase = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
                             static_cast<int64_t>(row) * p.o_sn;

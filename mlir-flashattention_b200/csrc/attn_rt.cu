@@ -8,7 +8,9 @@
 // device every entry point returns ATTN_ERR_NO_DEVICE.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -27,6 +29,16 @@ namespace {
 
 thread_local std::string g_last_error;
 std::atomic<int64_t> g_launches{0};
+
+// NVTX range over one entry point's host work (validation, staging copies,
+// launches), so that a timeline tool shows each call beside its kernels.
+// Header-only NVTX: without an attached tool the calls do nothing.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -73,6 +85,11 @@ struct DevState {
   std::mutex whole_mu;    // guards `whole` (held across one staged call)
   void* whole = nullptr;  // whole-operand staging of host f32 / dense-mask calls (grow-only)
   size_t whole_bytes = 0;
+  // Stream-ordered per-call scratch (dense-mask block classes, KV-split
+  // partials) comes from this pool, which keeps its memory between calls
+  // (release threshold unlimited): repeated calls do not map and unmap
+  // device memory, and each call's scratch stays private to its stream.
+  cudaMemPool_t pool = nullptr;
 };
 
 DevState g_dev[kMaxDevices];
@@ -102,6 +119,13 @@ int init_device(int device) {
     CUDA_TRY(cudaEventCreateWithFlags(&sb.comp_done, cudaEventDisableTiming));
     CUDA_TRY(cudaEventCreateWithFlags(&sb.d2h_done, cudaEventDisableTiming));
   }
+  cudaMemPoolProps pp{};
+  pp.allocType = cudaMemAllocationTypePinned;
+  pp.location.type = cudaMemLocationTypeDevice;
+  pp.location.id = device;
+  CUDA_TRY(cudaMemPoolCreate(&st.pool, &pp));
+  uint64_t keep = ~0ull;
+  CUDA_TRY(cudaMemPoolSetAttribute(st.pool, cudaMemPoolAttrReleaseThreshold, &keep));
   st.ready = true;
   return ATTN_OK;
 }
@@ -176,21 +200,97 @@ int sm_count(int* out) {
   return ATTN_OK;
 }
 
+// Stream-ordered scratch: from the current device's pool when the runtime
+// state is set up (attn_fwd, memref entries), else from the device's default
+// pool.  Freed with cudaFreeAsync on the same stream after the kernels.
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t s) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices && g_dev[dev].pool)
+    return cudaMallocFromPoolAsync(p, bytes, g_dev[dev].pool, s);
+  return cudaMallocAsync(p, bytes, s);
+}
+
+// KV tiles (of 128 keys) Q tile t of `pair` needs; the kernel's kv_counts.
+int pair_tiles(int pair, int t, int64_t Nq, int64_t Nk, bool causal) {
+  const int64_t nkv = (Nk + 127) / 128, qs = int64_t(pair) * 256 + 128 * t;
+  if (qs >= Nq) return 0;
+  if (!causal) return static_cast<int>(nkv);
+  return static_cast<int>(std::min<int64_t>(nkv, std::min<int64_t>(qs + 127, Nq - 1) / 128 + 1));
+}
+
+// Causal launches with few pairs per SM are bounded by their heaviest pairs,
+// which alone take longer than the average CTA's share (one head of
+// N = 16384: 64 pairs for 148 CTAs).  The kernel can run the S heaviest pair
+// indices of every slice as two halves of their KV tiles (merged in the
+// epilogue).  This picks S by replaying the kernel's work order and snake
+// assignment on the host and keeping the S with the shortest slowest CTA (0
+// unless that gains 2 %).  Costs, in KV steps of a pair: the item's steps,
+// +3 per item (Q load, pipeline start and drain, epilogue) and +4 more per
+// half (partial write, merge); fitted to B200 timings of 4 heads of
+// N = 16384 with S forced from 0 to 64 and of one such head, which the model
+// reproduces within 3 %.  Splitting then pays only with very few pairs per
+// SM (one head: 1.28x), not for 4 heads (256 pairs on 148 SMs).
+int choose_split(int num_bh, int num_pairs, int64_t Nq, int64_t Nk, int G) {
+  const int64_t W = int64_t(num_bh) * num_pairs;
+  if (num_pairs < 2 || W >= 4ll * G || G <= 0) return 0;
+  std::vector<int64_t> load(G);
+  std::vector<int> steps(num_pairs), mid(num_pairs);
+  for (int pr = 0; pr < num_pairs; ++pr) {
+    steps[pr] = std::max(pair_tiles(pr, 0, Nq, Nk, true), pair_tiles(pr, 1, Nq, Nk, true));
+    mid[pr] = (steps[pr] + 1) / 2;
+  }
+  auto makespan = [&](int S) {  // in KV steps
+    std::fill(load.begin(), load.end(), 0);
+    int64_t w = 0;
+    auto add = [&](int64_t cost, int count) {
+      for (int k = 0; k < count; ++k, ++w) {
+        const int64_t round = w / G, c = w % G;
+        load[(round & 1) ? G - 1 - c : c] += cost;
+      }
+    };
+    for (int j = 0; j < S; ++j) {
+      const int pr = num_pairs - 1 - j;
+      add(mid[pr] + 7, num_bh);
+      add(steps[pr] - mid[pr] + 7, num_bh);
+    }
+    for (int pr = num_pairs - 1 - S; pr >= 0; --pr) add(steps[pr] + 3, num_bh);
+    return *std::max_element(load.begin(), load.end());
+  };
+  const int64_t base = makespan(0);
+  int best = 0;
+  int64_t best_t = base;
+  const int step = std::max(1, num_pairs / 32);
+  for (int S = 1; S <= num_pairs; S += (S < 8 ? 1 : step)) {
+    const int64_t t = makespan(S);
+    if (t < best_t) {
+      best_t = t;
+      best = S;
+    }
+  }
+  return best_t * 50 < base * 49 ? best : 0;
+}
+
 // -------------------------------------------------------------- launches
 template <int D, int MODE, int ELT>
-int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
+int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream, bool may_split) {
   using C = attn_sm100::FwdCfg<D, ELT>;
   constexpr bool FP8 = C::FP8;
-  auto kern = attn_sm100::attn_fwd_sm100_kernel<D, MODE, ELT>;
+  constexpr bool kCausal = MODE == attn_sm100::kMaskCausal;
+  auto kern = attn_sm100::attn_fwd_sm100_kernel<D, MODE, ELT, false>;
+  // The causal mode also has the KV-split specialisation.
+  auto kern_split = attn_sm100::attn_fwd_sm100_kernel<D, MODE, ELT, kCausal>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   static int launch_regs = 0;
   std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(C::kSmemBytes));
-    cudaFuncAttributes fa{};
-    if (attr_err == cudaSuccess) attr_err = cudaFuncGetAttributes(&fa, kern);
-    launch_regs = fa.numRegs;
+    for (auto k : {kern, kern_split}) {
+      if (attr_err != cudaSuccess) break;
+      attr_err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(C::kSmemBytes));
+      cudaFuncAttributes fa{};
+      if (attr_err == cudaSuccess) attr_err = cudaFuncGetAttributes(&fa, k);
+      launch_regs = launch_regs == 0 ? fa.numRegs : std::min(launch_regs, fa.numRegs);
+    }
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute");
   // The kernel re-divides its registers between warpgroups (setmaxnreg); a
@@ -270,10 +370,10 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
     const size_t cls_bytes = r256(static_cast<size_t>(blocks));
     const size_t cnt_bytes = r256(static_cast<size_t>(Bm * Hm * nqt) * 4);
     const size_t w_bytes = r256(static_cast<size_t>(items) * 2);
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&cls),
-                                    cls_bytes + cnt_bytes + w_bytes + static_cast<size_t>(items) * 4,
-                                    stream);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync (mask tile classes)");
+    cudaError_t e = scratch_alloc(reinterpret_cast<void**>(&cls),
+                                  cls_bytes + cnt_bytes + w_bytes + static_cast<size_t>(items) * 4,
+                                  stream);
+    if (e != cudaSuccess) return cuda_fail(e, "stream-ordered scratch (mask tile classes)");
     int* row_count = reinterpret_cast<int*>(cls + cls_bytes);
     uint16_t* weights = reinterpret_cast<uint16_t*>(cls + cls_bytes + cnt_bytes);
     int* order = reinterpret_cast<int*>(cls + cls_bytes + cnt_bytes + w_bytes);
@@ -315,11 +415,35 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream) {
     if (cls) cudaFreeAsync(cls, stream);
     return rc;
   }
-  const int64_t items = static_cast<int64_t>(p.num_bh) * p.num_pairs;
+  // Causal KV split of the heaviest pairs when the schedule's tail needs it
+  // (never on the no-allocation path: its scratch is stream-ordered).
+  unsigned char* part = nullptr;
+  if (kCausal && may_split) p.split_pairs = choose_split(p.num_bh, p.num_pairs, d.Nq, d.Nk, sms);
+  if (p.split_pairs > 0) {
+    const size_t nsplit = static_cast<size_t>(p.split_pairs) * p.num_bh;
+    auto r256 = [](size_t n) { return (n + 255) / 256 * 256; };
+    const size_t o_bytes = r256(nsplit * 4 * 128 * D * sizeof(float));
+    const size_t l_bytes = r256(nsplit * 4 * 128 * sizeof(float));
+    const size_t c_bytes = r256(nsplit * 8 * sizeof(int));
+    cudaError_t e = scratch_alloc(reinterpret_cast<void**>(&part), o_bytes + l_bytes + c_bytes,
+                                  stream);
+    if (e != cudaSuccess) return cuda_fail(e, "stream-ordered scratch (KV-split partials)");
+    p.part_o = reinterpret_cast<float4*>(part);
+    p.part_lse = reinterpret_cast<float*>(part + o_bytes);
+    p.part_cnt = reinterpret_cast<int*>(part + o_bytes + l_bytes);
+    e = cudaMemsetAsync(p.part_cnt, 0, c_bytes, stream);
+    if (e != cudaSuccess) {
+      cudaFreeAsync(part, stream);
+      return cuda_fail(e, "cudaMemsetAsync (KV-split counters)");
+    }
+  }
+  const int64_t items = attn_sm100::work_items(p.num_bh, p.num_pairs, p.split_pairs);
   dim3 grid(static_cast<unsigned>(std::min<int64_t>(items, sms)));
-  kern<<<grid, attn_sm100::kThreads, C::kSmemBytes, stream>>>(mq, mk, mv, p);
+  (p.split_pairs > 0 ? kern_split : kern)<<<grid, attn_sm100::kThreads, C::kSmemBytes, stream>>>(
+      mq, mk, mv, p);
   cudaError_t e = cudaGetLastError();
   if (cls) cudaFreeAsync(cls, stream);
+  if (part) cudaFreeAsync(part, stream);
   if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_sm100 launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return ATTN_OK;
@@ -554,15 +678,18 @@ int validate(const AttnDesc& d) {
 }
 
 template <int D, int ELT>
-int dispatch_mode(const AttnDesc& d, int32_t* status, cudaStream_t s) {
+int dispatch_mode(const AttnDesc& d, int32_t* status, cudaStream_t s, bool may_split) {
   switch (d.mask_kind) {
-    case ATTN_MASK_CAUSAL: return launch_sm100<D, attn_sm100::kMaskCausal, ELT>(d, status, s);
-    case ATTN_MASK_DENSE: return launch_sm100<D, attn_sm100::kMaskDense, ELT>(d, status, s);
-    default: return launch_sm100<D, attn_sm100::kMaskNone, ELT>(d, status, s);
+    case ATTN_MASK_CAUSAL:
+      return launch_sm100<D, attn_sm100::kMaskCausal, ELT>(d, status, s, may_split);
+    case ATTN_MASK_DENSE:
+      return launch_sm100<D, attn_sm100::kMaskDense, ELT>(d, status, s, may_split);
+    default: return launch_sm100<D, attn_sm100::kMaskNone, ELT>(d, status, s, may_split);
   }
 }
 
-int dispatch(const AttnDesc& d, int32_t* status, cudaStream_t s) {
+// may_split = false: no stream-ordered scratch (the no-allocation entry).
+int dispatch(const AttnDesc& d, int32_t* status, cudaStream_t s, bool may_split = true) {
   if (d.dtype == ATTN_F32) {
     if ((d.D == 64 || d.D == 128) && f32_rows_aligned(d))
       return d.D == 64 ? launch_f32_tiled<64>(d, s) : launch_f32_tiled<128>(d, s);
@@ -572,12 +699,12 @@ int dispatch(const AttnDesc& d, int32_t* status, cudaStream_t s) {
   }
   using namespace attn_sm100;
   if (d.dtype == ATTN_BF16)
-    return d.D == 64 ? dispatch_mode<64, kEltBF16>(d, status, s)
-                     : dispatch_mode<128, kEltBF16>(d, status, s);
+    return d.D == 64 ? dispatch_mode<64, kEltBF16>(d, status, s, may_split)
+                     : dispatch_mode<128, kEltBF16>(d, status, s, may_split);
   if (d.dtype == ATTN_F16)
-    return d.D == 64 ? dispatch_mode<64, kEltF16>(d, status, s)
-                     : dispatch_mode<128, kEltF16>(d, status, s);
-  return dispatch_mode<128, kEltE4M3>(d, status, s);
+    return d.D == 64 ? dispatch_mode<64, kEltF16>(d, status, s, may_split)
+                     : dispatch_mode<128, kEltF16>(d, status, s, may_split);
+  return dispatch_mode<128, kEltE4M3>(d, status, s, may_split);
 }
 
 // ------------------------------------------------- memref-descriptor layer
@@ -695,6 +822,7 @@ bool packed4(const int64_t st[3], int64_t H, int64_t N, int64_t D) {
 // the kernels of chunk c and the D2H copy of chunk c-1 overlapped on three
 // streams.  Synchronous: returns when O (and LSE) are in host memory.
 int run_staged(const AttnDesc& hd, int device) {
+  NvtxRange range("attn_rt: host-memref staging");
   DevState& st = g_dev[device];
   std::lock_guard<std::mutex> lk(st.mu);  // one staged call per device at a time
   const size_t eb = elem_bytes(hd.dtype), ob = elem_bytes(hd.out_dtype);
@@ -776,7 +904,7 @@ int run_staged(const AttnDesc& hd, int device) {
       return fail(ATTN_ERR_UNSUPPORTED, "dense masks on host memrefs are not staged");
     int rc = validate(dd);
     if (rc != ATTN_OK) return rc;
-    rc = dispatch(dd, st.status, st.s_compute);
+    rc = dispatch(dd, st.status, st.s_compute, /*may_split=*/false);
     if (rc != ATTN_OK) return rc;
     CUDA_TRY(cudaEventRecord(sb.comp_done, st.s_compute));
     CUDA_TRY(cudaStreamWaitEvent(st.s_d2h, sb.comp_done, 0));
@@ -973,6 +1101,12 @@ const char* attn_rt_status_string(int code) {
 
 int attn_rt_init(int device) { return init_device(device); }
 
+int attn_rt_causal_split(int64_t slices, int64_t Nq, int64_t Nk, int sms) {
+  if (slices <= 0 || Nq <= 0 || Nk <= 0 || sms <= 0 || slices * ((Nq + 255) / 256) >= (1ll << 31))
+    return 0;
+  return choose_split(static_cast<int>(slices), static_cast<int>((Nq + 255) / 256), Nq, Nk, sms);
+}
+
 int attn_rt_probe_timeout(int64_t limit_ns) {
   if (limit_ns <= 0 || limit_ns > 2000000000ll)
     return fail(ATTN_ERR_INVALID, "probe limit must be in (0, 2 s]");
@@ -1001,6 +1135,7 @@ int attn_rt_check_status(int device, void* stream) {
 }
 
 int attn_fwd(const AttnDesc* desc, void* stream) {
+  NvtxRange range("attn_fwd");
   if (!desc) return fail(ATTN_ERR_INVALID, "null descriptor");
   bool no_rows = false, no_keys = false;
   int rc = check_empty(*desc, &no_rows, &no_keys);
@@ -1101,6 +1236,18 @@ int32_t _mlir_ciface_attn_fused_bf16_mask_4d(AttnMemRef4D* Q, AttnMemRef4D* K, A
                    view4(O, 2), scale, 1.f, 1.f, 1.f, LSE ? &L : nullptr, &M);
 }
 
+// The op's own mask form, i1 [seq_q, seq_k] (AttentionOps.td:26-28,40), on
+// rank-4 operands: one mask broadcast over every (batch, head) slice.
+int32_t _mlir_ciface_attn_fused_bf16_mask2d_4d(AttnMemRef4D* Q, AttnMemRef4D* K,
+                                               AttnMemRef4D* V, float scale, AttnMemRef2D* mask,
+                                               AttnMemRef4D* O, AttnMemRef4D* LSE) {
+  if (!Q || !K || !V || !O || !mask) return fail(ATTN_ERR_INVALID, "null memref descriptor");
+  View L, M = view2(mask, 1);  // extents 1 x 1 x seq_q x seq_k: broadcast
+  if (LSE) L = view4(LSE, 4);
+  return run_views(ATTN_BF16, ATTN_BF16, ATTN_MASK_DENSE, view4(Q, 2), view4(K, 2), view4(V, 2),
+                   view4(O, 2), scale, 1.f, 1.f, 1.f, LSE ? &L : nullptr, &M);
+}
+
 #define E4M3_4D(NAME, KIND)                                                                  \
   int32_t NAME(AttnMemRef4D* Q, AttnMemRef4D* K, AttnMemRef4D* V, float scale, float qd,     \
                float kd, float vd, AttnMemRef4D* O, AttnMemRef4D* LSE) {                     \
@@ -1131,29 +1278,39 @@ constexpr size_t kNoAllocStatusBytes = 256;  // status word, padded to 256 B
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 struct NoAllocDev {
-  std::once_flag once;
-  cudaError_t err = cudaSuccess;
+  std::mutex mu;
+  bool ready = false;            // set once the address below is known
   unsigned char* ptr = nullptr;  // device address of g_noalloc_scratch
-  int major = 0;
 };
 NoAllocDev g_noalloc[kMaxDevices];
 
 // Once per device, with that device current: check the architecture and
-// resolve the array's device address.  Allocates nothing.
+// resolve the array's device address.  Allocates nothing.  Only success is
+// remembered: a call that fails here (for instance one made inside a stream
+// capture) leaves the device unset, so a later call can try again.
 int noalloc_setup(int device, unsigned char** out) {
   if (device < 0 || device >= kMaxDevices) return fail(ATTN_ERR_INVALID, "bad device %d", device);
   NoAllocDev& nd = g_noalloc[device];
-  std::call_once(nd.once, [&] {
+  std::lock_guard<std::mutex> lock(nd.mu);
+  if (!nd.ready) {
     int major = 0;
-    nd.err = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
-    nd.major = major;
-    if (nd.err == cudaSuccess && major == 10)
-      nd.err = cudaGetSymbolAddress(reinterpret_cast<void**>(&nd.ptr), g_noalloc_scratch);
-  });
-  if (nd.err != cudaSuccess) return cuda_fail(nd.err, "attn_fwd_host_noalloc set-up");
-  if (nd.major != 10)
-    return fail(ATTN_ERR_NO_DEVICE, "device %d is not sm_100; attn_fwd_host_noalloc needs one",
-                device);
+    cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return cuda_fail(e, "attn_fwd_host_noalloc set-up: cudaDeviceGetAttribute");
+    }
+    if (major != 10)
+      return fail(ATTN_ERR_NO_DEVICE, "device %d is not sm_100; attn_fwd_host_noalloc needs one",
+                  device);
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return cuda_fail(e, "attn_fwd_host_noalloc set-up: cudaGetSymbolAddress");
+    }
+    nd.ptr = static_cast<unsigned char*>(p);
+    nd.ready = true;
+  }
   *out = nd.ptr;
   return ATTN_OK;
 }
@@ -1163,12 +1320,21 @@ size_t round256(size_t n) { return (n + 255) / 256 * 256; }
 }  // namespace
 
 extern "C" int attn_fwd_host_noalloc(const AttnDesc* desc, void* stream_) {
+  NvtxRange range("attn_fwd_host_noalloc");
   if (!desc) return fail(ATTN_ERR_INVALID, "null descriptor");
   const AttnDesc& hd = *desc;
   if (hd.mask_kind == ATTN_MASK_DENSE)
     return fail(ATTN_ERR_UNSUPPORTED, "attn_fwd_host_noalloc supports no-mask and causal calls");
   if (hd.q_descale_blocks || hd.k_descale_blocks || hd.v_descale_heads)
     return fail(ATTN_ERR_UNSUPPORTED, "attn_fwd_host_noalloc takes per-tensor descales only");
+  // Host buffers only: a device pointer here would be handed to host-to-
+  // device copies (or, without keys, written from the host).
+  const void* host_bufs[] = {hd.q, hd.k, hd.v, hd.o, hd.lse};
+  for (const void* ptr : host_bufs)
+    if (ptr && is_device_ptr(ptr))
+      return fail(ATTN_ERR_INVALID,
+                  "attn_fwd_host_noalloc takes host buffers; pass device-resident operands "
+                  "to attn_fwd");
   bool no_rows = false, no_keys = false;
   int rc = check_empty(hd, &no_rows, &no_keys);
   if (rc != ATTN_OK) return rc;
@@ -1177,8 +1343,20 @@ extern "C" int attn_fwd_host_noalloc(const AttnDesc* desc, void* stream_) {
     fill_no_keys_host(hd);
     return ATTN_OK;
   }
-  rc = validate(hd);
-  if (rc != ATTN_OK) return rc;
+  // Shape, type and scale rules only: every chunk is re-packed into dense,
+  // 256-byte aligned staging regions (validated again below), so the host
+  // buffers' own alignment and strides place no constraint on the kernel.
+  if (!hd.q || !hd.k || !hd.v || !hd.o)
+    return fail(ATTN_ERR_INVALID, "null Q/K/V/output pointer");
+  {
+    AttnDesc chk = hd;
+    alignas(256) static unsigned char aligned_dummy[256];
+    chk.q = chk.k = chk.v = chk.o = aligned_dummy;
+    chk.o_stride[2] = hd.D;
+    chk.o_stride[1] = hd.Nq * hd.D;
+    chk.o_stride[0] = hd.Hq * hd.Nq * hd.D;
+    if ((rc = validate(chk)) != ATTN_OK) return rc;
+  }
   int dev = 0;
   if ((rc = current_device(&dev)) != ATTN_OK) return rc;
   unsigned char* base = nullptr;
@@ -1207,9 +1385,26 @@ extern "C" int attn_fwd_host_noalloc(const AttnDesc* desc, void* stream_) {
   const int64_t per_chunk = std::min<int64_t>(ngroups, static_cast<int64_t>(room / per_group));
 
   int32_t* status = reinterpret_cast<int32_t*>(base);
+  // Once anything is enqueued, copies from and into the caller's buffers may
+  // be in flight: every error return after that point first waits for the
+  // stream, so the caller may free or reuse its buffers as soon as the call
+  // returns.
+#define NOALLOC_TRY(call)                            \
+  do {                                               \
+    cudaError_t e_ = (call);                         \
+    if (e_ != cudaSuccess) {                         \
+      const int c_ = cuda_fail(e_, #call);           \
+      cudaStreamSynchronize(s);                      \
+      return c_;                                     \
+    }                                                \
+  } while (0)
+  auto bail = [&](int code) {
+    cudaStreamSynchronize(s);
+    return code;
+  };
   // The array keeps the previous call's contents: the status word must start
   // at zero.  (Staging regions are fully overwritten before they are read.)
-  CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int32_t), s));
+  NOALLOC_TRY(cudaMemsetAsync(status, 0, sizeof(int32_t), s));
   unsigned char* dq = base + kNoAllocStatusBytes;
   unsigned char* dk = dq + round256(per_chunk * group * q_slice);
   unsigned char* dv = dk + round256(per_chunk * kv_slice);
@@ -1222,14 +1417,14 @@ extern "C" int attn_fwd_host_noalloc(const AttnDesc* desc, void* stream_) {
       const int64_t b = (g0 + g) / hd.Hkv, hk = (g0 + g) % hd.Hkv;
       const char* ks = static_cast<const char*>(hd.k) + (b * hd.k_stride[0] + hk * hd.k_stride[1]) * eb;
       const char* vs = static_cast<const char*>(hd.v) + (b * hd.v_stride[0] + hk * hd.v_stride[1]) * eb;
-      CUDA_TRY(cudaMemcpy2DAsync(dk + g * kv_slice, hd.D * eb, ks, hd.k_stride[2] * eb,
+      NOALLOC_TRY(cudaMemcpy2DAsync(dk + g * kv_slice, hd.D * eb, ks, hd.k_stride[2] * eb,
                                  hd.D * eb, hd.Nk, cudaMemcpyHostToDevice, s));
-      CUDA_TRY(cudaMemcpy2DAsync(dv + g * kv_slice, hd.D * eb, vs, hd.v_stride[2] * eb,
+      NOALLOC_TRY(cudaMemcpy2DAsync(dv + g * kv_slice, hd.D * eb, vs, hd.v_stride[2] * eb,
                                  hd.D * eb, hd.Nk, cudaMemcpyHostToDevice, s));
       for (int64_t i = 0; i < group; ++i) {
         const int64_t h = hk * group + i;
         const char* qs = static_cast<const char*>(hd.q) + (b * hd.q_stride[0] + h * hd.q_stride[1]) * eb;
-        CUDA_TRY(cudaMemcpy2DAsync(dq + (g * group + i) * q_slice, hd.D * eb, qs,
+        NOALLOC_TRY(cudaMemcpy2DAsync(dq + (g * group + i) * q_slice, hd.D * eb, qs,
                                    hd.q_stride[2] * eb, hd.D * eb, hd.Nq,
                                    cudaMemcpyHostToDevice, s));
       }
@@ -1245,24 +1440,25 @@ extern "C" int attn_fwd_host_noalloc(const AttnDesc* desc, void* stream_) {
     dd.k_stride[2] = hd.D; dd.k_stride[1] = hd.Nk * hd.D; dd.k_stride[0] = hd.Nk * hd.D;
     dd.v_stride[2] = hd.D; dd.v_stride[1] = hd.Nk * hd.D; dd.v_stride[0] = hd.Nk * hd.D;
     dd.status = status;
-    if ((rc = validate(dd)) != ATTN_OK) return rc;
-    if ((rc = dispatch(dd, status, s)) != ATTN_OK) return rc;
+    if ((rc = validate(dd)) != ATTN_OK) return bail(rc);
+    if ((rc = dispatch(dd, status, s, /*may_split=*/false)) != ATTN_OK) return bail(rc);
     for (int64_t g = 0; g < gn; ++g) {
       const int64_t b = (g0 + g) / hd.Hkv, hk = (g0 + g) % hd.Hkv;
       for (int64_t i = 0; i < group; ++i) {
         const int64_t h = hk * group + i;
         char* os = static_cast<char*>(hd.o) + (b * hd.o_stride[0] + h * hd.o_stride[1]) * ob;
-        CUDA_TRY(cudaMemcpy2DAsync(os, hd.o_stride[2] * ob, dout + (g * group + i) * o_slice,
+        NOALLOC_TRY(cudaMemcpy2DAsync(os, hd.o_stride[2] * ob, dout + (g * group + i) * o_slice,
                                    hd.D * ob, hd.D * ob, hd.Nq, cudaMemcpyDeviceToHost, s));
         if (hd.lse)
-          CUDA_TRY(cudaMemcpyAsync(hd.lse + (b * hd.Hq + h) * hd.Nq, dl + (g * group + i) * hd.Nq,
+          NOALLOC_TRY(cudaMemcpyAsync(hd.lse + (b * hd.Hq + h) * hd.Nq, dl + (g * group + i) * hd.Nq,
                                    sizeof(float) * hd.Nq, cudaMemcpyDeviceToHost, s));
       }
     }
   }
   int32_t code = 0;
-  CUDA_TRY(cudaMemcpyAsync(&code, status, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-  CUDA_TRY(cudaStreamSynchronize(s));
+  NOALLOC_TRY(cudaMemcpyAsync(&code, status, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  NOALLOC_TRY(cudaStreamSynchronize(s));
+#undef NOALLOC_TRY
   if (code != 0) return fail(code, "kernel reported %s", attn_rt_status_string(code));
   return ATTN_OK;
 }

@@ -18,8 +18,10 @@ def AttentionToRuntimePass : Pass<"attention-to-runtime", "::mlir::ModuleOp"> {
     llvm.emit_c_interface so that the lowered program calls
     _mlir_ciface_attn_fused_* in libattnrt.so.  The variant is chosen from the
     mask operand: none -> nomask, a causal generic (j > i) -> causal, any
-    other i1 mask -> mask (rank-2 f32 only).  Use instead of --tiling-pass.
+    other i1 mask -> mask (rank-2 f32, rank-4 bf16) or mask2d (a rank-2
+    mask on rank-4 bf16 operands).  The returned status is checked with
+    cf.assert.  Use instead of --tiling-pass.
   }];
   let dependentDialects = ["::mlir::func::FuncDialect", "::mlir::memref::MemRefDialect",
-                           "::mlir::arith::ArithDialect"];
+                           "::mlir::arith::ArithDialect", "::mlir::cf::ControlFlowDialect"];
 }

@@ -10,12 +10,18 @@
 // (include/Attention/AttentionOps.td:20-54) into
 //
 //   %rc = func.call @attn_fused_<dtype>_<variant>[_4d](%Q, %K, %V, %s, [%m,] %O)
+//   %ok = arith.cmpi eq, %rc, %c0_i32 : i32
+//   cf.assert %ok, "attention.fused: runtime call failed ..."
 //
 // where the callee is declared `func.func private ... attributes
 // {llvm.emit_c_interface}` so that, after the standard lowering to LLVM, the
 // call lands on `_mlir_ciface_attn_fused_*` in libattnrt.so (include/attn_rt.h).
 // The runtime launches the sm_100a kernels; the op's semantics (in-place write
-// of %O, AttentionOps.cpp:15-30) are unchanged.
+// of %O, AttentionOps.cpp:15-30) are unchanged.  The runtime reports failures
+// (shape, alignment, CUDA errors, a device timeout) as a negative i32 rather
+// than aborting; the reference op has no error result, so the lowered program
+// checks the code with cf.assert and stops with a message instead of
+// continuing with a stale %O.
 //
 // Mask classification (the reference's mask-specialisation design,
 // Design.md:402-444, which its code does not implement):
@@ -26,7 +32,10 @@
 //     (the causal generic), or a mask value carrying the unit attribute
 //     `attention.causal` on its defining op                -> "causal"
 //   * anything else                                      -> "mask" (dense i1
-//     operand; rank-2 f32 or rank-4 bf16, others rejected with an error)
+//     operand; rank-2 f32 or rank-4 bf16, others rejected with an error).
+//     On rank-4 bf16 operands the op's own [seq_q, seq_k] mask (rank 2,
+//     AttentionOps.td:26-28,40) calls "mask2d" (one mask for every slice);
+//     a rank-4 mask calls "mask".
 //
 // Shapes: every memref operand is passed through `memref.cast` to the fully
 // dynamic strided type of its rank (memref<?x?xT, strided<[?, ?], offset: ?>>),
@@ -46,6 +55,7 @@
 #include "Attention/AttentionOps.h"
 #include "Attention/AttentionPasses.h"
 #include "mlir/Dialect/Arith/IR/Arith.h"
+#include "mlir/Dialect/ControlFlow/IR/ControlFlowOps.h"
 #include "mlir/Dialect/Func/IR/FuncOps.h"
 #include "mlir/Dialect/Linalg/IR/Linalg.h"
 #include "mlir/Dialect/MemRef/IR/MemRef.h"
@@ -152,11 +162,21 @@ struct FusedToRuntimeCall : public OpRewritePattern<FusedOp> {
     if (kind == MaskKind::Dense && !((dt == "f32" && rank == 2) || (dt == "bf16" && rank == 4)))
       return op.emitOpError("a general i1 mask is supported for rank-2 f32 and rank-4 bf16 "
                             "operands");
+    // A dense mask is the op's [seq_q, seq_k] (rank 2) or, on rank-4
+    // operands, a per-slice [B, H, seq_q, seq_k]; each rank has its own entry
+    // so the runtime reads a descriptor of the rank it was given.
+    const int64_t maskRank =
+        op.getMask() ? cast<MemRefType>(op.getMask().getType()).getRank() : 0;
+    if (kind == MaskKind::Dense && maskRank != 2 && maskRank != rank)
+      return op.emitOpError("mask must be rank 2 [seq_q, seq_k] or of the operands' rank");
     if (dt != "f32" && rank != 4)
       return op.emitOpError("bf16/f16/e4m3 operands are lowered in their rank-4 form");
 
     std::string callee = ("attn_fused_" + dt + "_").str();
-    callee += kind == MaskKind::None ? "nomask" : kind == MaskKind::Causal ? "causal" : "mask";
+    callee += kind == MaskKind::None     ? "nomask"
+              : kind == MaskKind::Causal ? "causal"
+              : (rank == 4 && maskRank == 2) ? "mask2d"
+                                             : "mask";
     if (rank == 4) callee += "_4d";
 
     auto module = op->getParentOfType<ModuleOp>();
@@ -213,7 +233,14 @@ struct FusedToRuntimeCall : public OpRewritePattern<FusedOp> {
     for (size_t i = 3; i < memrefs.size(); ++i) args.push_back(toDyn(memrefs[i], dynTypes[i]));
     if (dt != "f32")
       args.push_back(toDyn(rewriter.create<memref::AllocaOp>(op.getLoc(), lseT), lseDyn));
-    rewriter.create<func::CallOp>(op.getLoc(), fn, args);
+    auto call = rewriter.create<func::CallOp>(op.getLoc(), fn, args);
+    Value zero = rewriter.create<arith::ConstantIntOp>(op.getLoc(), 0, 32);
+    Value ok = rewriter.create<arith::CmpIOp>(op.getLoc(), arith::CmpIPredicate::eq,
+                                              call.getResult(0), zero);
+    rewriter.create<cf::AssertOp>(
+        op.getLoc(), ok,
+        ("attention.fused: runtime call " + callee +
+         " failed (negative ATTN_ERR_* code; attn_rt_last_error() has the message)"));
     rewriter.eraseOp(op);
     return success();
   }

@@ -9,9 +9,13 @@
 // CHECK-DAG: func.func private @attn_fused_f32_nomask(memref<?x?xf32, strided<[?, ?], offset: ?>>, memref<?x?xf32, strided<[?, ?], offset: ?>>, memref<?x?xf32, strided<[?, ?], offset: ?>>, f32, memref<?x?xf32, strided<[?, ?], offset: ?>>) -> i32 attributes {llvm.emit_c_interface}
 // CHECK-DAG: func.func private @attn_fused_f32_mask(memref<?x?xf32, strided<[?, ?], offset: ?>>, memref<?x?xf32, strided<[?, ?], offset: ?>>, memref<?x?xf32, strided<[?, ?], offset: ?>>, f32, memref<?x?xi1, strided<[?, ?], offset: ?>>, memref<?x?xf32, strided<[?, ?], offset: ?>>) -> i32 attributes {llvm.emit_c_interface}
 // CHECK-DAG: func.func private @attn_fused_bf16_causal_4d(memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, f32, memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, memref<?x?x?x?xf32, strided<[?, ?, ?, ?], offset: ?>>) -> i32 attributes {llvm.emit_c_interface}
+// CHECK-DAG: func.func private @attn_fused_bf16_mask2d_4d(memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, f32, memref<?x?xi1, strided<[?, ?], offset: ?>>, memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, memref<?x?x?x?xf32, strided<[?, ?, ?, ?], offset: ?>>) -> i32 attributes {llvm.emit_c_interface}
+// CHECK-DAG: func.func private @attn_fused_bf16_mask_4d(memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, f32, memref<?x?x?x?xi1, strided<[?, ?, ?, ?], offset: ?>>, memref<?x?x?x?xbf16, strided<[?, ?, ?, ?], offset: ?>>, memref<?x?x?x?xf32, strided<[?, ?, ?, ?], offset: ?>>) -> i32 attributes {llvm.emit_c_interface}
 // CHECK-LABEL: func.func @plain
 // CHECK:       memref.cast %{{.*}} : memref<64x32xf32> to memref<?x?xf32, strided<[?, ?], offset: ?>>
-// CHECK:       call @attn_fused_f32_nomask
+// CHECK:       %[[RC:.*]] = call @attn_fused_f32_nomask
+// CHECK:       %[[OK:.*]] = arith.cmpi eq, %[[RC]], %{{.*}} : i32
+// CHECK:       cf.assert %[[OK]], "attention.fused: runtime call attn_fused_f32_nomask failed
 // CHECK-NOT:   attention.fused
 func.func @plain(%Q: memref<64x32xf32>, %K: memref<64x32xf32>, %V: memref<64x32xf32>,
                  %s: f32, %O: memref<64x32xf32>) {
@@ -83,5 +87,33 @@ func.func @bf16_causal(%Q: memref<1x32x16384x128xbf16>, %K: memref<1x32x16384x12
   attention.fused ins(%Q, %K, %V : memref<1x32x16384x128xbf16>, memref<1x32x16384x128xbf16>,
                                    memref<1x32x16384x128xbf16>)
     scale(%s : f32) mask(%m : memref<16384x16384xi1>) outs(%O : memref<1x32x16384x128xbf16>)
+  return
+}
+
+// Rank-4 bf16 operands with the op's own rank-2 dense mask [seq_q, seq_k]:
+// the mask keeps its rank-2 descriptor and goes to the mask2d entry, which
+// applies it to every (batch, head) slice.
+// CHECK-LABEL: func.func @bf16_dense_rank2_mask
+// CHECK:       memref.cast %{{.*}} : memref<300x300xi1> to memref<?x?xi1, strided<[?, ?], offset: ?>>
+// CHECK:       %[[RC:.*]] = call @attn_fused_bf16_mask2d_4d
+// CHECK:       cf.assert
+func.func @bf16_dense_rank2_mask(%Q: memref<1x2x300x64xbf16>, %K: memref<1x2x300x64xbf16>,
+                                 %V: memref<1x2x300x64xbf16>, %m: memref<300x300xi1>,
+                                 %O: memref<1x2x300x64xbf16>, %s: f32) {
+  attention.fused ins(%Q, %K, %V : memref<1x2x300x64xbf16>, memref<1x2x300x64xbf16>,
+                                   memref<1x2x300x64xbf16>)
+    scale(%s : f32) mask(%m : memref<300x300xi1>) outs(%O : memref<1x2x300x64xbf16>)
+  return
+}
+
+// A per-slice rank-4 mask keeps the rank-4 mask entry.
+// CHECK-LABEL: func.func @bf16_dense_rank4_mask
+// CHECK:       call @attn_fused_bf16_mask_4d
+func.func @bf16_dense_rank4_mask(%Q: memref<1x2x300x64xbf16>, %K: memref<1x2x300x64xbf16>,
+                                 %V: memref<1x2x300x64xbf16>, %m: memref<1x2x300x300xi1>,
+                                 %O: memref<1x2x300x64xbf16>, %s: f32) {
+  attention.fused ins(%Q, %K, %V : memref<1x2x300x64xbf16>, memref<1x2x300x64xbf16>,
+                                   memref<1x2x300x64xbf16>)
+    scale(%s : f32) mask(%m : memref<1x2x300x300xi1>) outs(%O : memref<1x2x300x64xbf16>)
   return
 }

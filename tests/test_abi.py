@@ -119,17 +119,21 @@ def _pass_callees():
                             "RuntimeLoweringPass.cpp")).read()
     assert 'std::string callee = ("attn_fused_" + dt + "_").str();' in src
     assert '(dt == "f32" && rank == 2) || (dt == "bf16" && rank == 4)' in src
+    assert '(rank == 4 && maskRank == 2) ? "mask2d"' in src
+    assert "cf::AssertOp" in src  # the returned status is checked
     out = []
     for dt in ("f32", "bf16", "f16", "e4m3"):
         for rank in (2, 4):
             if dt != "f32" and rank != 4:
                 continue
-            for kind in ("nomask", "causal", "mask"):
+            for kind in ("nomask", "causal", "mask", "mask2d"):
                 if kind == "mask" and not ((dt == "f32" and rank == 2) or (dt == "bf16" and rank == 4)):
                     continue
+                if kind == "mask2d" and not (dt == "bf16" and rank == 4):
+                    continue  # a rank-2 mask on rank-4 bf16 operands
                 name = f"attn_fused_{dt}_{kind}" + ("_4d" if rank == 4 else "")
-                nargs = 4 + (3 if dt == "e4m3" else 0) + (1 if kind == "mask" else 0) + 1 + \
-                    (1 if dt != "f32" else 0)
+                nargs = 4 + (3 if dt == "e4m3" else 0) + (1 if kind.startswith("mask") else 0) + \
+                    1 + (1 if dt != "f32" else 0)
                 out.append((name, nargs))
     return out
 
@@ -139,7 +143,7 @@ def test_every_call_the_lowering_pass_emits_is_declared_with_its_arity():
     protos = {m.group(1): m.group(2) for m in
               re.finditer(r"_mlir_ciface_(\w+)\s*\(([^;{]*)\)\s*;", text)}
     callees = _pass_callees()
-    assert len(callees) == 12
+    assert len(callees) == 13
     for name, nargs in callees:
         assert name in protos, name
         assert protos[name].count(",") + 1 == nargs, (name, protos[name])

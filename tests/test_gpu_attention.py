@@ -164,16 +164,20 @@ def test_strided_operands_match_contiguous(pkg, wl):
 
 def test_host_memref_pipeline_equals_device(pkg, wl):
     """The memref entry with pinned HOST buffers (staged, overlapped copies)
-    gives bit-identical results to the device-resident call."""
-    w = wl.Workload("t", "bf16", 2, 8, 8, 512, 128, True, seed=9)
+    gives bit-identical results to the device-resident call.  Host-buffer
+    entries never split KV ranges, so the shape is one whose device call
+    does not split either (296 slices x 2 pairs: enough work per SM)."""
+    w = wl.Workload("t", "bf16", 2, 148, 148, 512, 128, True, seed=9)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert pkg.lib().attn_rt_causal_split(2 * 148, 512, 512, sms) == 0
     inp = wl.make_inputs(w)
     q, k, v = wl.to_device(inp, w)
-    L_dev = torch.empty((2, 8, 512), dtype=torch.float32, device="cuda")
+    L_dev = torch.empty((2, 148, 512), dtype=torch.float32, device="cuda")
     ref = pkg.fused(q, k, v, w.scale, causal=True, lse=L_dev)
     pkg.check_status(0)
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
     ho = torch.empty_like(hq).pin_memory()
-    hl = torch.empty((2, 8, 512, 1), dtype=torch.float32).pin_memory()
+    hl = torch.empty((2, 148, 512, 1), dtype=torch.float32).pin_memory()
     L = pkg.lib()
     rc = L._mlir_ciface_attn_fused_bf16_causal_4d(
         pkg.memref(hq), pkg.memref(hk), pkg.memref(hv), w.scale, pkg.memref(ho), pkg.memref(hl))
@@ -275,15 +279,18 @@ def test_dense_causal_mask_equals_causal_variant(pkg, wl, D):
     exact zeros."""
     import ctypes
 
-    w = wl.Workload("t", "bf16", 1, 4, 4, 640, D, True, seed=8)
+    H = 200  # enough pairs per SM that the causal call runs no KV split
+    w = wl.Workload("t", "bf16", 1, H, H, 640, D, True, seed=8)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert pkg.lib().attn_rt_causal_split(H, 640, 640, sms) == 0
     inp = wl.make_inputs(w)
     q, k, v = wl.to_device(inp, w)
     a = pkg.fused(q, k, v, w.scale, causal=True)
-    m8 = torch.ones(640, 640, dtype=torch.uint8, device="cuda").triu(1).expand(1, 4, 640, 640)
+    m8 = torch.ones(640, 640, dtype=torch.uint8, device="cuda").triu(1).expand(1, H, 640, 640)
     out = torch.empty_like(a)
     d = pkg.AttnDesc()
     d.dtype, d.out_dtype, d.mask_kind = pkg.ATTN_BF16, pkg.ATTN_BF16, pkg.MASK_DENSE
-    d.B, d.Hq, d.Hkv, d.Nq, d.Nk, d.D = 1, 4, 4, 640, 640, D
+    d.B, d.Hq, d.Hkv, d.Nq, d.Nk, d.D = 1, H, H, 640, 640, D
     for dst, t in ((d.q_stride, q), (d.k_stride, k), (d.v_stride, v), (d.o_stride, out)):
         dst[0], dst[1], dst[2] = t.stride(0), t.stride(1), t.stride(2)
     d.q, d.k, d.v, d.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
@@ -350,6 +357,43 @@ def test_bf16_mask_memref_with_host_buffers(pkg, wl, oracle):
     ref, _ = oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale,
                                  mask=np.broadcast_to(M, (1, 2, 300, 300)))
     assert _rel(o.float().numpy(), ref) <= 2e-2
+
+
+def test_rank2_mask_on_rank4_operands_as_the_pass_calls_it(pkg, wl, oracle):
+    """The lowering pass's call for the op's own rank-2 mask [seq_q, seq_k]
+    on rank-4 bf16 operands: _mlir_ciface_attn_fused_bf16_mask2d_4d with a
+    2-D mask descriptor (host memrefs), equal bit for bit to the rank-4 mask
+    entry given the same mask as [1, 1, seq_q, seq_k], and to the oracle."""
+    w = wl.Workload("t", "bf16", 2, 2, 2, 300, 64, False, seed=13)
+    inp = wl.make_inputs(w)
+    rng = np.random.default_rng(5)
+    M = rng.random((300, 300)) < 0.4
+    M[:, 0] = False
+    q, k, v = (t.cpu() for t in wl.to_device(inp, w))
+    m2 = torch.from_numpy(M.astype(np.uint8))
+    o2, o4 = torch.empty_like(q), torch.empty_like(q)
+    l2 = torch.empty((2, 2, 300, 1), dtype=torch.float32)
+    l4 = torch.empty_like(l2)
+    L = pkg.lib()
+    rc = L._mlir_ciface_attn_fused_bf16_mask2d_4d(
+        pkg.memref(q), pkg.memref(k), pkg.memref(v), w.scale, pkg.memref(m2), pkg.memref(o2),
+        pkg.memref(l2))
+    assert rc == 0, pkg.last_error()
+    rc = L._mlir_ciface_attn_fused_bf16_mask_4d(
+        pkg.memref(q), pkg.memref(k), pkg.memref(v), w.scale, pkg.memref(m2.reshape(1, 1, 300, 300)),
+        pkg.memref(o4), pkg.memref(l4))
+    assert rc == 0, pkg.last_error()
+    assert torch.equal(o2, o4) and torch.equal(l2, l4)
+    ref, ref_lse = oracle.attn_batched(inp.qf, inp.kf, inp.vf, w.scale,
+                                       mask=np.broadcast_to(M, (2, 2, 300, 300)))
+    assert _rel(o2.float().numpy(), ref) <= 2e-2
+    assert np.abs(l2[..., 0].numpy() - ref_lse).max() <= 1e-3
+    # A mask whose extents do not match the operands is refused, not misread.
+    bad = torch.zeros((300, 299), dtype=torch.uint8)
+    rc = L._mlir_ciface_attn_fused_bf16_mask2d_4d(
+        pkg.memref(q), pkg.memref(k), pkg.memref(v), w.scale, pkg.memref(bad), pkg.memref(o2),
+        pkg.memref(l2))
+    assert rc == -2
 
 
 def test_bounded_wait_times_out_and_device_stays_usable(pkg, wl, oracle):
@@ -609,13 +653,13 @@ def test_device_resident_memrefs_via_runtime_helpers(pkg, wl):
     as the host-memref call."""
     import ctypes
 
-    w = wl.Workload("t", "bf16", 1, 4, 4, 300, 128, True, seed=23)
+    w = wl.Workload("t", "bf16", 1, 4, 4, 300, 128, False, seed=23)
     inp = wl.make_inputs(w)
     q, k, v = (t.cpu().contiguous() for t in wl.to_device(inp, w))
     ho = torch.empty_like(q)
     L = pkg.lib()
     lse0 = torch.empty((0, 0, 0, 1), dtype=torch.float32)
-    rc = L._mlir_ciface_attn_fused_bf16_causal_4d(pkg.memref(q), pkg.memref(k), pkg.memref(v),
+    rc = L._mlir_ciface_attn_fused_bf16_nomask_4d(pkg.memref(q), pkg.memref(k), pkg.memref(v),
                                                   w.scale, pkg.memref(ho), pkg.memref(lse0))
     assert rc == 0, pkg.last_error()
     nbytes = q.numel() * 2
@@ -632,7 +676,7 @@ def test_device_resident_memrefs_via_runtime_helpers(pkg, wl):
         m.allocated = m.aligned = ptr
         return m
 
-    rc = L._mlir_ciface_attn_fused_bf16_causal_4d(
+    rc = L._mlir_ciface_attn_fused_bf16_nomask_4d(
         dev_memref(ptrs[0], q), dev_memref(ptrs[1], k), dev_memref(ptrs[2], v), w.scale,
         dev_memref(ptrs[3], ho), pkg.memref(lse0))
     assert rc == 0, pkg.last_error()
