@@ -26,8 +26,9 @@
 //               query row reads its S row from TMEM, applies the mask, updates
 //               (m, l) in registers, writes P (bf16 / f16 / e4m3) back into the
 //               S columns (d = 64: P's own columns) and rescales its O row in
-//               TMEM when m moved; at the end of a pair it writes O / l and
-//               the LSE.
+//               TMEM when m moved; at the end of a pair it writes O / l
+//               (through a shared-memory box per warp and a TMA tensor
+//               store) and the LSE.
 //   warps 10-11 idle (they complete warpgroup 2 for the register split).
 //   The two Q tiles ping-pong: while one softmax group works, the tensor
 //   cores run the other tile's GEMMs.  Registers: launched at 168 per thread
@@ -139,8 +140,11 @@ struct FwdCfg {
   // S_t GEMM starts as soon as the softmax has read S_t ("early S").
   static constexpr bool kEarlyS = D == 64 && !FP8;
   static constexpr int kNumBars = 2 + 2 * kStages + 2 + 2 + 2 + 2 + 2 + 1;
-  static constexpr size_t kSmemBytes =
-      1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes + kNumBars * 8 + 16;
+  // Epilogue staging: one 32-row x 128-byte box (128-byte swizzle) per
+  // softmax warp, written from registers and stored to O by TMA.
+  static constexpr int kStageBox = 32 * 128;
+  static constexpr size_t kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes +
+                                       kStages * kTileBytes + 8 * kStageBox + kNumBars * 8 + 16;
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
   static_assert(kNBox >= 1, "tile must span at least one 128-byte box");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -372,7 +376,8 @@ template <int D, int MODE, int ELT, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
-                          const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+                          const __grid_constant__ CUtensorMap tmV,
+                          const __grid_constant__ CUtensorMap tmO, const FwdParams p) {
   constexpr bool CAUSAL = MODE == kMaskCausal;
   static_assert(!SPLIT || CAUSAL, "the KV split is a causal-mode schedule");
   constexpr bool DENSE = MODE == kMaskDense;
@@ -383,7 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + 2 * C::kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + C::kStages * C::kTileBytes);
+  uint8_t* sStage = sKV + C::kStages * C::kTileBytes;  // 1024-byte aligned
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + 8 * C::kStageBox);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;
   uint64_t* kv_full = bars + 2;
@@ -1074,47 +1080,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const float inv_l = nan_row ? __int_as_float(0x7fc00000) : p.o_scale * vd / l;
-      const int64_t obase = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh +
-                            static_cast<int64_t>(row) * p.o_sn;
-      const bool live = row < p.Nq;
+      // O leaves through this warp's staging box: each thread writes its row's
+      // 128-byte slice (8 x 16 bytes, 128-byte swizzle: chunk c of row r at
+      // chunk position c ^ (r & 7), conflict-free), then one lane stores the
+      // 32 x 128-byte box with TMA; rows past Nq fall outside the tensor and
+      // are not written.  The previous box's store must have read the buffer.
+      {
+        uint8_t* stg = sStage + warp * C::kStageBox;
+        const bool f32o = p.out_kind == 1;
+        const int cols = f32o ? 32 : 64;  // columns of O per 128-byte box
+        const int y = qs + quarter * 32;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += cols) {
+          uint32_t w[32];  // the row's 128 bytes
+          if (f32o) {
+            uint32_t o[32];
+            tmem_ld32(tO + c0, o);
+            tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + c * 32, o);
-        tmem_wait_ld();
-        if (c == D / 32 - 1) {
-          // O_t has been read into registers: the next pair may overwrite it.
-          tc_fence_before();
-          mbar_arrive(&o_free[t]);
-        }
-        if (live) {
-          if (p.out_kind == 1) {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.o) + obase + c * 32);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l,
-                                   __uint_as_float(o[4 * i + 1]) * inv_l,
-                                   __uint_as_float(o[4 * i + 2]) * inv_l,
-                                   __uint_as_float(o[4 * i + 3]) * inv_l);
+            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(o[i]) * inv_l);
           } else {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.o) + obase + c * 32);
+            uint32_t o[32], o2[32];
+            tmem_ld32(tO + c0, o);
+            tmem_ld32(tO + c0 + 32, o2);
+            tmem_wait_ld();
             const bool f16 = p.out_kind == 2;
-            auto pk2 = [&](int e) {
-              const float a = __uint_as_float(o[e]) * inv_l, bb = __uint_as_float(o[e + 1]) * inv_l;
-              return f16 ? pack_f16(a, bb) : pack_bf16(a, bb);
-            };
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 v;
-              v.x = pk2(8 * i + 0);
-              v.y = pk2(8 * i + 2);
-              v.z = pk2(8 * i + 4);
-              v.w = pk2(8 * i + 6);
-              dst[i] = v;
+            for (int i = 0; i < 16; ++i) {
+              const float a0 = __uint_as_float(o[2 * i]) * inv_l, a1 = __uint_as_float(o[2 * i + 1]) * inv_l;
+              const float b0 = __uint_as_float(o2[2 * i]) * inv_l, b1 = __uint_as_float(o2[2 * i + 1]) * inv_l;
+              w[i] = f16 ? pack_f16(a0, a1) : pack_bf16(a0, a1);
+              w[16 + i] = f16 ? pack_f16(b0, b1) : pack_bf16(b0, b1);
             }
+          }
+          if (c0 + cols >= D) {
+            // O_t has been read into registers: the next pair may overwrite it.
+            tc_fence_before();
+            mbar_arrive(&o_free[t]);
+          }
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) * 16)) =
+                make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_4d(&tmO, stg, c0, y, h, b);
+            bulk_commit_group();
           }
         }
       }
+      const bool live = row < p.Nq;
       if (live && p.lse)
         p.lse[static_cast<int64_t>(itm.bh) * p.Nq + row] =
             nan_row ? __int_as_float(0x7fc00000) : (m + __log2f(l)) * 0.69314718055994531f;
@@ -1122,6 +1140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ---------------------------------------------------------------- teardown
+  if (warp < 8 && lane == 0) bulk_wait_all();  // this warp's O stores are complete
   tc_fence_before();
   __syncthreads();
   if (warp == 9) {

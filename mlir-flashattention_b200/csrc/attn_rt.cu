@@ -159,8 +159,11 @@ EncodeTiledFn encode_fn() {
 // 4-D map over (head_dim, rows, heads, batch) with a 128-byte x 128-row box
 // and 128-byte swizzle.  Strides in elements; a unit dimension gets a
 // synthetic stride (never stepped along).
+// 4-D tensor map [B, H, N, D] (element strides), 128-byte swizzle; the box
+// is 128 bytes of D by `box_rows` rows.
 int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int eb, int64_t D,
-             int64_t N, int64_t H, int64_t B, int64_t s_n, int64_t s_h, int64_t s_b) {
+             int64_t N, int64_t H, int64_t B, int64_t s_n, int64_t s_h, int64_t s_b,
+             int box_rows = 128) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(ATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   if (N == 1) s_n = D;
@@ -174,7 +177,7 @@ int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int eb,
     if (strides[i] % 16 != 0 || strides[i] >= (1ull << 40))
       return fail(ATTN_ERR_ALIGN, "tensor stride %llu bytes is not a multiple of 16",
                   static_cast<unsigned long long>(strides[i]));
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / eb), 128, 1, 1};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / eb), static_cast<cuuint32_t>(box_rows), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -315,6 +318,14 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream, bool m
   if ((rc = make_map(&mv, d.v, dt, eb, d.D, d.Nk, d.Hkv, d.B, d.v_stride[2], d.v_stride[1],
                      d.v_stride[0])) != ATTN_OK)
     return rc;
+  // O is written by TMA tensor stores of 32-row boxes (one per softmax warp).
+  CUtensorMap mo;
+  const CUtensorMapDataType dto = d.out_dtype == ATTN_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                  : d.out_dtype == ATTN_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if ((rc = make_map(&mo, d.o, dto, d.out_dtype == ATTN_F32 ? 4 : 2, d.D, d.Nq, d.Hq, d.B,
+                     d.o_stride[2], d.o_stride[1], d.o_stride[0], 32)) != ATTN_OK)
+    return rc;
   attn_sm100::FwdParams p{};
   p.o = d.o;
   p.o_sb = d.o_stride[0];
@@ -440,7 +451,7 @@ int launch_sm100(const AttnDesc& d, int32_t* status, cudaStream_t stream, bool m
   const int64_t items = attn_sm100::work_items(p.num_bh, p.num_pairs, p.split_pairs);
   dim3 grid(static_cast<unsigned>(std::min<int64_t>(items, sms)));
   (p.split_pairs > 0 ? kern_split : kern)<<<grid, attn_sm100::kThreads, C::kSmemBytes, stream>>>(
-      mq, mk, mv, p);
+      mq, mk, mv, mo, p);
   cudaError_t e = cudaGetLastError();
   if (cls) cudaFreeAsync(cls, stream);
   if (part) cudaFreeAsync(part, stream);
