@@ -104,3 +104,34 @@ def test_ragged_cross_attention_split(pkg, oracle, H, Nq, Nk, dt):
     ref, ref_lse = oracle.attn_batched(qf, kf, vf, D ** -0.5, causal=True)
     assert _rel(out.float().cpu().numpy(), ref) <= tol
     assert np.abs(L.cpu().numpy() - ref_lse).max() <= 1e-3
+
+
+def test_e4m3_per_block_descales_with_split(pkg, wl, oracle):
+    """Per-block Q/K and per-head V e4m3 factors on a split launch: the second
+    half of a pair starts at its own KV block's factor, so a wrong start block
+    shows up as a large error (block magnitudes spread over two decades)."""
+    B, Hq, Hkv, N, D = 1, 2, 1, 4096, 128
+    assert pkg.lib().attn_rt_causal_split(B * Hq, N, N, _sms()) > 0
+    rng = np.random.default_rng(23)
+
+    def spread(H):
+        f = 10.0 ** rng.uniform(-1.0, 1.0, size=(B, H, N // 128))
+        return np.repeat(f, 128, axis=2)[:, :, :, None].astype(np.float32)
+
+    q = rng.standard_normal((B, Hq, N, D)).astype(np.float32) * spread(Hq)
+    k = rng.standard_normal((B, Hkv, N, D)).astype(np.float32) * spread(Hkv)
+    v = rng.standard_normal((B, Hkv, N, D)).astype(np.float32)
+    q8, qd, qf = wl.quant_e4m3_blocks(q)
+    k8, kd, kf = wl.quant_e4m3_blocks(k)
+    v8, vd, vf = wl.quant_e4m3_heads(v)
+    scale = 1.0 / np.sqrt(D)
+    dev = [torch.from_numpy(a).cuda() for a in (q8, k8, v8, qd, kd, vd)]
+    L = torch.empty((B, Hq, N), dtype=torch.float32, device="cuda")
+    out = pkg.fused(dev[0], dev[1], dev[2], scale, causal=True, lse=L, q_descale=dev[3],
+                    k_descale=dev[4], v_descale=dev[5])
+    pkg.check_status(0)
+    got = out.float().cpu().numpy()
+    ref, ref_lse = oracle.attn_batched(qf, kf, vf, scale, causal=True)
+    for h in range(Hq):
+        assert _rel(got[0, h], ref[0, h]) <= 6e-2, h
+    assert (np.abs(L.cpu().numpy() - ref_lse) <= 1e-2 + 1e-4 * np.abs(ref_lse)).all()
