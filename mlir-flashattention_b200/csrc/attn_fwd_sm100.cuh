@@ -19,7 +19,8 @@
 //               KV tile of the pair's list (PairSched); each S GEMM is
 //               issued once the P·V GEMM reading P from its TMEM columns has
 //               completed (gate_S).
-//               d = 64 ("early S", P in columns of its own): S_0(j'), S_1(j')
+//               d = 64 ("early S", P in columns of its own) and e4m3 (early
+//               S, P in shared memory, P·V in the SS form): S_0(j'), S_1(j')
 //               as soon as each softmax has read its S, then P·V_0(j),
 //               P·V_1(j).
 //   warps 0-3   softmax for Q tile 0, warps 4-7 for Q tile 1: one thread per
@@ -36,7 +37,8 @@
 //   theirs to 224 and warpgroup 2 lowers its to 56 (setmaxnreg).
 //
 // TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,256+D)
-// O1 [256+D, 256+2D); at d = 64 P0 [384,448) P1 [448,512).  Exponentials are base 2 with the scale folded in:
+// O1 [256+D, 256+2D); at d = 64 P0 [384,448) P1 [448,512); e4m3 P_t is a
+// 128 x 128-byte shared-memory tile.  Exponentials are base 2 with the scale folded in:
 // p = 2^(s·scale·log2e − m).  The running max only moves when it grows by
 // more than 2^8 (values of p stay <= 256, exact in bf16/e4m3 range), which
 // skips most O rescales; the final O/l and LSE are unaffected by the choice.
@@ -135,16 +137,22 @@ struct FwdCfg {
   static constexpr uint32_t kFmt = ELT == kEltBF16 ? 1u : 0u;
   static constexpr int kKind = FP8 ? 1 : 0;
   // TMEM: S_t at columns 128 t, O_t at 256 + D t.  At d = 128 the columns
-  // are all taken and P_t overwrites S_t, so the next S_t GEMM follows the
-  // P·V GEMM; at d = 64, P_t has its own columns (384 + 64 t) and the next
-  // S_t GEMM starts as soon as the softmax has read S_t ("early S").
-  static constexpr bool kEarlyS = D == 64 && !FP8;
+  // are all taken: bf16 / f16 P_t overwrites S_t, so the next S_t GEMM
+  // follows the P·V GEMM.  At d = 64, P_t has its own columns (384 + 64 t);
+  // e4m3 P_t (128 x 128 bytes) lives in shared memory and its P·V GEMM takes
+  // the SS form.  In both the next S_t GEMM starts as soon as the softmax
+  // has read S_t ("early S").
+  static constexpr bool kPSmem = FP8;
+  static constexpr bool kEarlyS = D == 64 || kPSmem;
+  static constexpr int kPTile = 128 * 128;  // e4m3 P_t: 128 rows x 128 keys
+  static constexpr int kPBytes = kPSmem ? 2 * kPTile : 0;
   static constexpr int kNumBars = 2 + 2 * kStages + 2 + 2 + 2 + 2 + 2 + 1;
   // Epilogue staging: one 32-row x 128-byte box (128-byte swizzle) per
   // softmax warp, written from registers and stored to O by TMA.
   static constexpr int kStageBox = 32 * 128;
   static constexpr size_t kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes +
-                                       kStages * kTileBytes + 8 * kStageBox + kNumBars * 8 + 16;
+                                       kStages * kTileBytes + 8 * kStageBox + kPBytes +
+                                       kNumBars * 8 + 16;
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
   static_assert(kNBox >= 1, "tile must span at least one 128-byte box");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -389,7 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + 2 * C::kTileBytes;
   uint8_t* sStage = sKV + C::kStages * C::kTileBytes;  // 1024-byte aligned
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + 8 * C::kStageBox);
+  uint8_t* sP = sStage + 8 * C::kStageBox;              // e4m3 P tiles (1024-byte aligned)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::kPBytes);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;
   uint64_t* kv_full = bars + 2;
@@ -536,12 +545,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto issue_PV = [&](int t, int stage, bool acc) {
         const uint64_t b0 = dV0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
-        const uint32_t tP = tmem + (C::kEarlyS ? 384 + t * 64 : t * 128);  // P_t's columns
+        if constexpr (C::kPSmem) {
+          // P_t from shared memory (K-major, 128-byte swizzle, one 128-byte
+          // row per query row): each MMA takes the next 32 keys' bytes.
+          const uint64_t a0 = make_sdesc(smem_u32(sP + t * C::kPTile), 16, 1024);
   #pragma unroll
-        for (int kk = 0; kk < C::kKStepsPV; ++kk)
-          mma_ts_lead<C::kKind>(lead, tmem + 256 + t * D, tP + kk * 8,
-                                b0 + static_cast<uint64_t>((kk * C::kKeysPerStep * 128) >> 4), idO,
-                                (acc || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < C::kKStepsPV; ++kk)
+            mma_ss_lead<C::kKind>(lead, tmem + 256 + t * D,
+                                  a0 + static_cast<uint64_t>((kk * 32) >> 4),
+                                  b0 + static_cast<uint64_t>((kk * C::kKeysPerStep * 128) >> 4),
+                                  idO, (acc || kk > 0) ? 1u : 0u);
+        } else {
+          const uint32_t tP = tmem + (C::kEarlyS ? 384 + t * 64 : t * 128);  // P_t's columns
+  #pragma unroll
+          for (int kk = 0; kk < C::kKStepsPV; ++kk)
+            mma_ts_lead<C::kKind>(lead, tmem + 256 + t * D, tP + kk * 8,
+                                  b0 + static_cast<uint64_t>((kk * C::kKeysPerStep * 128) >> 4),
+                                  idO, (acc || kk > 0) ? 1u : 0u);
+        }
       };
       auto wait = [&](uint64_t* bar, int phase) {
         return warp_wait(bar, static_cast<uint32_t>(phase & 1), abort_flag, p.status);
@@ -975,7 +996,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc1 = f2_add(acc1, f2_pack(s[4 * c + 2], s[4 * c + 3]));
             pk[c] = pack_e4m3x4(s[4 * c], s[4 * c + 1], s[4 * c + 2], s[4 * c + 3]);
           }
-          tmem_st32(tP + 0, pk);
+          // P_t's shared-memory tile and O_t: the previous P·V GEMM of this
+          // tile reads the one and accumulates into the other.
+          if (steps > 0 && !warp_wait(&pv_done[t], static_cast<uint32_t>((steps - 1) & 1),
+                                      abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // The row's 128 bytes as 8 chunks of 16 (128-byte swizzle: chunk c
+          // of row r at position c ^ (r & 7), conflict-free), then made
+          // visible to the tensor core (async proxy) before the warp's
+          // arrival on p_ready.
+          uint8_t* prow = sP + t * C::kPTile + r * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          fence_proxy_async_smem();
         }
         float q0, q1;
         f2_unpack(f2_add(acc0, acc1), q0, q1);
