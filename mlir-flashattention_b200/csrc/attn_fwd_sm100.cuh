@@ -129,7 +129,9 @@ struct FwdCfg {
   static constexpr int kNBox = (D * kEB) / 128;         // 128-byte column boxes per tile
   static constexpr int kBoxBytes = 128 * 128;           // 128 rows x 128 bytes
   static constexpr int kTileBytes = kNBox * kBoxBytes;  // one 128-row tile
-  static constexpr int kStages = (FP8 || D == 64) ? 8 : 4;
+  // K / V ring depth (tiles of 128 keys): 4 at bf16 / f16 d = 128, 8 at
+  // d = 64, 6 at e4m3 (whose two P buffers per Q tile take the room of two).
+  static constexpr int kStages = FP8 ? 6 : (D == 64 ? 8 : 4);
   static constexpr int kKStepsS = (D * kEB) / 32;       // 32 bytes of K per MMA
   static constexpr int kKeysPerStep = 32 / kEB;         // keys per P·V MMA
   static constexpr int kKStepsPV = 128 / kKeysPerStep;
@@ -144,9 +146,17 @@ struct FwdCfg {
   // has read S_t ("early S").
   static constexpr bool kPSmem = FP8;
   static constexpr bool kEarlyS = D == 64 || kPSmem;
-  static constexpr int kPTile = 128 * 128;  // e4m3 P_t: 128 rows x 128 keys
-  static constexpr int kPBytes = kPSmem ? 2 * kPTile : 0;
-  static constexpr int kNumBars = 2 + 2 * kStages + 2 + 2 + 2 + 2 + 2 + 1;
+  // e4m3 P: two 128 rows x 128 keys tiles per Q tile, P of step n in
+  // buffer n & 1.  The P·V GEMM that last read a buffer (step n - 2) was
+  // issued before the S GEMM of step n, and the commit that completes S of
+  // step n tracks every earlier MMA of the issuing thread: once the softmax
+  // has seen S of step n, the buffer is free.
+  static constexpr int kPTile = 128 * 128;
+  static constexpr int kPBytes = kPSmem ? 4 * kPTile : 0;
+  // q_full, q_empty, the K / V ring, s_full[2], p_ready[4] and pv_done[4]
+  // (e4m3: one per tile and P buffer; otherwise [t]), o_free[2], s_free[2],
+  // drain.
+  static constexpr int kNumBars = 2 + 2 * kStages + 2 + 4 + 4 + 2 + 2 + 1;
   // Epilogue staging: one 32-row x 128-byte box (128-byte swizzle) per
   // softmax warp, written from registers and stored to O by TMA.
   static constexpr int kStageBox = 32 * 128;
@@ -405,9 +415,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* kv_empty = kv_full + C::kStages;
   uint64_t* s_full = kv_empty + C::kStages;
   uint64_t* p_ready = s_full + 2;
-  uint64_t* pv_done = p_ready + 2;
-  uint64_t* o_free = pv_done + 2;
+  uint64_t* pv_done = p_ready + 4;
+  uint64_t* o_free = pv_done + 4;
   uint64_t* s_free = o_free + 2;  // early S: the softmax has read S_t
+  // P of step n of tile t ready / P·V GEMM n of tile t complete, and the
+  // parity of that phase.  e4m3 has one barrier of each per P buffer (n & 1):
+  // its softmax waits for a P·V GEMM only before an O rescale, so it may run
+  // a step ahead of the MMA warp, and with one barrier per buffer no waiter
+  // is ever two phases away from the barrier it waits on (P of step n + 2
+  // needs S of step n + 2, which the MMA warp issues only after the P·V GEMM
+  // of step n).
+  auto p_bar = [&](int t, int n) { return FP8 ? &p_ready[2 * t + (n & 1)] : &p_ready[t]; };
+  auto pv_bar = [&](int t, int n) { return FP8 ? &pv_done[2 * t + (n & 1)] : &pv_done[t]; };
+  auto ph_par = [](int n) { return static_cast<uint32_t>((FP8 ? (n >> 1) : n) & 1); };
   uint64_t* drain = s_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -428,7 +448,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
       mbar_init(&p_ready[t], 4);  // one arrival per softmax warp
+      mbar_init(&p_ready[2 + t], 4);
       mbar_init(&pv_done[t], 1);
+      mbar_init(&pv_done[2 + t], 1);
       mbar_init(&o_free[t], 128);
       mbar_init(&s_free[t], 4);  // one arrival per softmax warp
     }
@@ -543,12 +565,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_PV = [&](int t, int stage, bool acc) {
+      // pbuf: the P buffer of this step (e4m3 P in shared memory).
+      auto issue_PV = [&](int t, int stage, bool acc, int pbuf) {
         const uint64_t b0 = dV0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
         if constexpr (C::kPSmem) {
           // P_t from shared memory (K-major, 128-byte swizzle, one 128-byte
           // row per query row): each MMA takes the next 32 keys' bytes.
-          const uint64_t a0 = make_sdesc(smem_u32(sP + t * C::kPTile), 16, 1024);
+          const uint64_t a0 = make_sdesc(smem_u32(sP + (2 * t + pbuf) * C::kPTile), 16, 1024);
   #pragma unroll
           for (int kk = 0; kk < C::kKStepsPV; ++kk)
             mma_ss_lead<C::kKind>(lead, tmem + 256 + t * D,
@@ -645,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             for (int t = 0; t < 2 && ok; ++t) {
               if (!(DENSE ? act_kt[t] : sc.act(t, kt))) continue;
-              if (!wait(&p_ready[t], p_cnt[t])) {
+              if (!warp_wait(p_bar(t, p_cnt[t]), ph_par(p_cnt[t]), abort_flag, p.status)) {
                 ok = false;
                 break;
               }
@@ -655,9 +678,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
               }
               tc_fence_after();
-              issue_PV(t, slot(vpos), !first_pv[t]);
+              issue_PV(t, slot(vpos), !first_pv[t], (p_cnt[t] - 1) & 1);
               first_pv[t] = false;
-              mma_commit_lead(lead, &pv_done[t]);
+              mma_commit_lead(lead, pv_bar(t, p_cnt[t] - 1));
             }
             if (!ok) break;
             mma_commit_lead(lead, &kv_empty[slot(vpos)]);  // V free once the P·V GEMMs finish
@@ -747,7 +770,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
               }
               tc_fence_after();
-              issue_PV(t, vst(i), !first_pv[t]);
+              issue_PV(t, vst(i), !first_pv[t], 0);
               first_pv[t] = false;
               mma_commit_lead(lead, &pv_done[t]);
               ++pv_cnt[t];
@@ -996,19 +1019,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc1 = f2_add(acc1, f2_pack(s[4 * c + 2], s[4 * c + 3]));
             pk[c] = pack_e4m3x4(s[4 * c], s[4 * c + 1], s[4 * c + 2], s[4 * c + 3]);
           }
-          // P_t's shared-memory tile and O_t: the previous P·V GEMM of this
-          // tile reads the one and accumulates into the other.
-          if (steps > 0 && !warp_wait(&pv_done[t], static_cast<uint32_t>((steps - 1) & 1),
-                                      abort_flag, p.status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // The row's 128 bytes as 8 chunks of 16 (128-byte swizzle: chunk c
-          // of row r at position c ^ (r & 7), conflict-free), then made
-          // visible to the tensor core (async proxy) before the warp's
-          // arrival on p_ready.
-          uint8_t* prow = sP + t * C::kPTile + r * 128;
+          // P buffer steps & 1 is free (see kPTile); the row's 128 bytes as 8
+          // chunks of 16 (128-byte swizzle: chunk c of row r at position
+          // c ^ (r & 7), conflict-free), then made visible to the tensor core
+          // (async proxy) before the warp's arrival on p_ready.
+          uint8_t* prow = sP + (2 * t + (steps & 1)) * C::kPTile + r * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c)
             *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) =
@@ -1021,6 +1036,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool need = !first && (alpha != 1.f);
         first = false;
         if (__any_sync(0xffffffffu, need)) {
+          if constexpr (FP8) {
+            // O_t: the previous P·V GEMM of this tile accumulates into it.
+            if (!warp_wait(pv_bar(t, steps - 1), ph_par(steps - 1), abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t o[32];
@@ -1034,13 +1057,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_ready[t]);
+        if (lane == 0) mbar_arrive(p_bar(t, steps));
         kt = kn;
       }
       if (!ok) break;
       // -------------------------------------------------------- epilogue
-      if (!warp_wait(&pv_done[t], static_cast<uint32_t>((steps - 1) & 1), abort_flag,
-                     p.status)) {
+      // The tile's last P·V GEMM has completed.
+      if (!warp_wait(pv_bar(t, steps - 1), ph_par(steps - 1), abort_flag, p.status)) {
         ok = false;
         break;
       }
