@@ -1062,6 +1062,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // -------------------------------------------------------- epilogue
+      const float inv_l = nan_row ? __int_as_float(0x7fc00000) : p.o_scale * vd / l;
       // The tile's last P·V GEMM has completed.
       if (!warp_wait(pv_bar(t, steps - 1), ph_par(steps - 1), abort_flag, p.status)) {
         ok = false;
@@ -1140,7 +1141,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           continue;
         }
       }
-      const float inv_l = nan_row ? __int_as_float(0x7fc00000) : p.o_scale * vd / l;
       // O leaves through this warp's staging box: each thread writes its row's
       // 128-byte slice (8 x 16 bytes, 128-byte swizzle: chunk c of row r at
       // chunk position c ^ (r & 7), conflict-free), then one lane stores the
@@ -1148,37 +1148,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // are not written.  The previous box's store must have read the buffer.
       {
         uint8_t* stg = sStage + warp * C::kStageBox;
-        const bool f32o = p.out_kind == 1;
-        const int cols = f32o ? 32 : 64;  // columns of O per 128-byte box
         const int y = qs + quarter * 32;
-#pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += cols) {
-          uint32_t w[32];  // the row's 128 bytes
-          if (f32o) {
-            uint32_t o[32];
-            tmem_ld32(tO + c0, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(o[i]) * inv_l);
-          } else {
-            uint32_t o[32], o2[32];
-            tmem_ld32(tO + c0, o);
-            tmem_ld32(tO + c0 + 32, o2);
-            tmem_wait_ld();
-            const bool f16 = p.out_kind == 2;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float a0 = __uint_as_float(o[2 * i]) * inv_l, a1 = __uint_as_float(o[2 * i + 1]) * inv_l;
-              const float b0 = __uint_as_float(o2[2 * i]) * inv_l, b1 = __uint_as_float(o2[2 * i + 1]) * inv_l;
-              w[i] = f16 ? pack_f16(a0, a1) : pack_bf16(a0, a1);
-              w[16 + i] = f16 ? pack_f16(b0, b1) : pack_bf16(b0, b1);
-            }
-          }
-          if (c0 + cols >= D) {
-            // O_t has been read into registers: the next pair may overwrite it.
-            tc_fence_before();
-            mbar_arrive(&o_free[t]);
-          }
+        // Stage the 32 words of one 128-byte box and store it with TMA.
+        auto store_box = [&](const uint32_t (&w)[32], int c0) {
           if (lane == 0) bulk_wait_read_all();
           __syncwarp();
 #pragma unroll
@@ -1190,6 +1162,68 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) {
             tma_store_4d(&tmO, stg, c0, y, h, b);
             bulk_commit_group();
+          }
+        };
+        if (p.out_kind != 1) {
+          const bool f16 = p.out_kind == 2;
+          // 64 columns of the row (two TMEM chunks) scaled and packed.
+          auto pack_box = [&](const uint32_t(&lo)[32], const uint32_t(&hi)[32], uint32_t(&w)[32]) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float a0 = __uint_as_float(lo[2 * i]) * inv_l, a1 = __uint_as_float(lo[2 * i + 1]) * inv_l;
+              const float b0 = __uint_as_float(hi[2 * i]) * inv_l, b1 = __uint_as_float(hi[2 * i + 1]) * inv_l;
+              w[i] = f16 ? pack_f16(a0, a1) : pack_bf16(a0, a1);
+              w[16 + i] = f16 ? pack_f16(b0, b1) : pack_bf16(b0, b1);
+            }
+          };
+          if constexpr (!FP8) {
+            // bf16 / f16 inputs: the whole O row in one TMEM round trip, O_t
+            // released to the next pair at once, then one box per 64 columns
+            // (c3 +1.8 %; the e4m3 kernel measured faster with the per-box
+            // form below).
+            uint32_t o[D / 32][32];
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) tmem_ld32(tO + c * 32, o[c]);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&o_free[t]);
+#pragma unroll
+            for (int c0 = 0; c0 < D; c0 += 64) {
+              uint32_t w[32];
+              pack_box(o[c0 / 32], o[c0 / 32 + 1], w);
+              store_box(w, c0);
+            }
+          } else {
+#pragma unroll 1
+            for (int c0 = 0; c0 < D; c0 += 64) {
+              uint32_t lo[32], hi[32], w[32];
+              tmem_ld32(tO + c0, lo);
+              tmem_ld32(tO + c0 + 32, hi);
+              tmem_wait_ld();
+              if (c0 + 64 >= D) {
+                // O_t has been read into registers: the next pair may overwrite it.
+                tc_fence_before();
+                mbar_arrive(&o_free[t]);
+              }
+              pack_box(lo, hi, w);
+              store_box(w, c0);
+            }
+          }
+        } else {
+          // f32: 32 columns per box.
+#pragma unroll 1
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t o[32], w[32];
+            tmem_ld32(tO + c0, o);
+            tmem_wait_ld();
+            if (c0 + 32 >= D) {
+              // O_t has been read into registers: the next pair may overwrite it.
+              tc_fence_before();
+              mbar_arrive(&o_free[t]);
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(o[i]) * inv_l);
+            store_box(w, c0);
           }
         }
       }
