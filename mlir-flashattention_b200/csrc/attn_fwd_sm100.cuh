@@ -836,10 +836,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float mask_val = pos ? -INFINITY : INFINITY;
     int steps = 0;  // S tiles consumed so far (s_full / pv_done phases)
     bool ok = true;
+    // e4m3: the next work item, decoded ahead while the epilogue waits for
+    // the last P·V GEMM (c5 +2 %; the bf16 / f16 kernels' wait is shorter and
+    // measured slower with the extra work in front of it).
+    int pre_rr = -1, pre_w = -1;
+    Item pre_itm;
     for (int rr = 0; ok; ++rr) {
-      const int w = item_index<CAUSAL>(rr, cta, G, W);
+      int w;
+      Item itm0;
+      if (pre_rr == rr) {
+        w = pre_w;
+        itm0 = pre_itm;
+      } else {
+        w = item_index<CAUSAL>(rr, cta, G, W);
+        if (w >= 0)
+          itm0 = decode_item<CAUSAL, SPLIT>(DENSE ? __ldg(p.order + w) : w, p.num_bh,
+                                             p.num_pairs, p.split_pairs);
+      }
       if (w < 0) break;
-      const Item itm = decode_item<CAUSAL, SPLIT>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs, p.split_pairs);
+      const Item itm = itm0;
       const PairSched<MODE, SPLIT> sc = make_sched<MODE, SPLIT>(itm, p);
       const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq;
       const int qs = itm.pair * 256 + 128 * t;
@@ -1062,7 +1077,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // -------------------------------------------------------- epilogue
+      // Work that does not read O, done while the last P·V GEMM completes:
+      // 1/l and (e4m3) the row's LSE and the next work item.  A split pair's
+      // halves merge their LSE below.
       const float inv_l = nan_row ? __int_as_float(0x7fc00000) : p.o_scale * vd / l;
+      auto store_lse = [&]() {
+        if (!(SPLIT && sc.merge[t]) && row < p.Nq && p.lse)
+          p.lse[static_cast<int64_t>(itm.bh) * p.Nq + row] =
+              nan_row ? __int_as_float(0x7fc00000) : (m + __log2f(l)) * 0.69314718055994531f;
+      };
+      if constexpr (FP8) {
+        store_lse();
+        pre_rr = rr + 1;
+        pre_w = item_index<CAUSAL>(pre_rr, cta, G, W);
+        if (pre_w >= 0)
+          pre_itm = decode_item<CAUSAL, SPLIT>(DENSE ? __ldg(p.order + pre_w) : pre_w, p.num_bh,
+                                               p.num_pairs, p.split_pairs);
+      }
       // The tile's last P·V GEMM has completed.
       if (!warp_wait(pv_bar(t, steps - 1), ph_par(steps - 1), abort_flag, p.status)) {
         ok = false;
@@ -1227,10 +1258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      const bool live = row < p.Nq;
-      if (live && p.lse)
-        p.lse[static_cast<int64_t>(itm.bh) * p.Nq + row] =
-            nan_row ? __int_as_float(0x7fc00000) : (m + __log2f(l)) * 0.69314718055994531f;
+      if constexpr (!FP8) store_lse();
     }
   }
 
