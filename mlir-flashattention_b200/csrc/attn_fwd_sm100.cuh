@@ -37,8 +37,9 @@
 //   theirs to 224 and warpgroup 2 lowers its to 56 (setmaxnreg).
 //
 // TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,256+D)
-// O1 [256+D, 256+2D); at d = 64 P0 [384,448) P1 [448,512); e4m3 P_t is a
-// 128 x 128-byte shared-memory tile.  Exponentials are base 2 with the scale folded in:
+// O1 [256+D, 256+2D); at d = 64 P0 [384,448) P1 [448,512); e4m3 P_t lives
+// in two 128 x 128-byte shared-memory tiles (step n in tile n & 1).
+// Exponentials are base 2 with the scale folded in:
 // p = 2^(s·scale·log2e − m).  The running max only moves when it grows by
 // more than 2^8 (values of p stay <= 256, exact in bf16/e4m3 range), which
 // skips most O rescales; the final O/l and LSE are unaffected by the choice.
