@@ -149,6 +149,47 @@ def test_e4m3_block_descales(pkg, wl, oracle, causal, nq, nk):
         pkg.fused(bf, bf, bf, 0.1, q_descale=torch.ones((1, 1, 1), device="cuda"))
 
 
+@pytest.mark.parametrize("dtype,D", [("bf16", 128), ("bf16", 64), ("e4m3", 128)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_running_max_rescales(pkg, wl, oracle, dtype, D, causal):
+    """Scores that grow along the keys (each KV tile's row max 15-35 log2
+    units above the previous one), so the running max moves past the rescale
+    threshold at nearly every step: O is rescaled in TMEM again and again
+    (the e4m3 kernel waits for the previous P·V GEMM only then)."""
+    rng = np.random.default_rng(80 + D + (dtype == "e4m3"))
+    B, H, N = 1, 2, 640
+    u = rng.standard_normal(D).astype(np.float32)
+    u /= np.linalg.norm(u)
+    ramp = np.linspace(0.0, 4.0, N, dtype=np.float32)
+    q = (200.0 * u + rng.standard_normal((B, H, N, D))).astype(np.float32)
+    k = (ramp[:, None] * u + 0.3 * rng.standard_normal((B, H, N, D))).astype(np.float32)
+    v = rng.standard_normal((B, H, N, D)).astype(np.float32)
+    scale = 1.0 / np.sqrt(D)
+    L = torch.empty((B, H, N), dtype=torch.float32, device="cuda")
+    if dtype == "e4m3":
+        (q8, qd, qf), (k8, kd, kf), (v8, vd, vf) = (wl.quant_e4m3(a) for a in (q, k, v))
+        dev = [torch.from_numpy(a).view(torch.float8_e4m3fn).cuda() for a in (q8, k8, v8)]
+        out = pkg.fused(*dev, scale, causal=causal, lse=L, q_descale=qd, k_descale=kd,
+                        v_descale=vd)
+        tol, ltol = 6e-2, 1e-2
+    else:
+        qf, kf, vf = (wl.round_bf16(a) for a in (q, k, v))
+        dev = [torch.from_numpy(a).to(torch.bfloat16).cuda() for a in (qf, kf, vf)]
+        out = pkg.fused(*dev, scale, causal=causal, lse=L)
+        tol, ltol = 2e-2, 1e-3
+    pkg.check_status(0)
+    ref, ref_lse = oracle.attn_batched(qf, kf, vf, scale, causal=causal)
+    got = out.float().cpu().numpy()
+    for h in range(H):
+        assert _rel(got[0, h], ref[0, h]) <= tol, h
+    lse = L.cpu().numpy()
+    assert (np.abs(lse - ref_lse) <= ltol + 1e-4 * np.abs(ref_lse)).all()
+    # The scores really do climb by more than the threshold across KV tiles.
+    s = (qf[0, 0] @ kf[0, 0].T) * scale * np.log2(np.e)
+    tile_max = s[-1].reshape(-1, 128).max(axis=1)
+    assert (np.diff(tile_max) > 8.0).all()
+
+
 def test_strided_operands_match_contiguous(pkg, wl):
     """A [B, N, H, D] buffer viewed as [B, H, N, D] (non-contiguous heads)."""
     w = wl.Workload("t", "bf16", 2, 4, 4, 256, 128, True, seed=5)
