@@ -45,9 +45,41 @@ def attention_fused(q, k, v, scale, mask=None):
     """The op the pass emits: ``attention.fused ins(q, k, v) scale(scale)
     [mask(mask)]`` with a freshly allocated output (bf16 for bf16 / e4m3
     inputs, f16 for f16, f32 for f32), as returned by this package's
-    ``fused``.  ``mask`` is bool with True = masked."""
+    ``fused``.  ``mask`` is bool with True = masked.
+
+    A traced graph carries no shapes, so the pass cannot check ranks: any
+    leading dims shared by q, k and v (and a mask over them, or a [Nq, Nk]
+    one) are flattened into the head dim of ``fused``'s [1, H, N, D] form,
+    and the result takes q's shape back."""
     from . import fused  # noqa: PLC0415  (the package imports this module lazily)
-    return fused(q, k, v, float(scale), mask=mask)
+    q4, k4, v4, m4, lead = _as_4d(q, k, v, mask)
+    out = fused(q4, k4, v4, float(scale), mask=m4)
+    return out if lead is None else out.reshape(*lead, *out.shape[-2:])
+
+
+def _as_4d(q, k, v, mask):
+    """q, k, v (and the mask) in a rank ``fused`` takes, and q's leading dims
+    to restore (None when nothing was reshaped)."""
+    from . import VerifyError  # noqa: PLC0415
+
+    if q.dim() in (2, 4) and k.dim() == q.dim() and v.dim() == q.dim() and \
+            (mask is None or mask.dim() in (2, q.dim())):
+        return q, k, v, mask, None
+    lead = tuple(q.shape[:-2])
+    if q.dim() < 2 or tuple(k.shape[:-2]) != lead or tuple(v.shape[:-2]) != lead:
+        raise VerifyError("attention.fused: Q, K and V need the same leading dims "
+                          "(rank 2 or 4 otherwise)")
+    h = 1
+    for d in lead:
+        h *= d
+    q4, k4, v4 = (t.reshape(1, h, *t.shape[-2:]) for t in (q, k, v))
+    m4 = mask
+    if mask is not None and mask.dim() > 2:
+        if tuple(mask.shape[:-2]) != lead:
+            raise VerifyError("attention.fused: the mask must be [seq_q, seq_k] or share "
+                              "Q's leading dims")
+        m4 = mask.reshape(1, h, *mask.shape[-2:])
+    return q4, k4, v4, m4, lead
 
 
 _MATMULS = {operator.matmul, torch.matmul, torch.bmm}

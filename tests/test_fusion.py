@@ -131,6 +131,33 @@ def test_shared_transpose_is_kept(fusion):
     assert "transpose" in targets and torch.softmax not in targets
 
 
+def test_leading_dims_flattened_for_the_op(fusion, monkeypatch):
+    """Ranks other than 2 and 4 reach the op as [1, H, N, D] (leading dims
+    flattened into heads) and come back in q's shape; mismatched leading
+    dims are a VerifyError."""
+    import mlir_flashattention_b200 as pkg_mod
+
+    seen = {}
+
+    def fake_fused(q, k, v, scale, mask=None):
+        seen.update(q=tuple(q.shape), k=tuple(k.shape), mask=None if mask is None else tuple(mask.shape))
+        return torch.zeros(q.shape)
+
+    monkeypatch.setattr(pkg_mod, "fused", fake_fused)
+    q = torch.zeros(3, 5, 40, 64)[0]          # rank 3: [5, 40, 64]
+    k = v = torch.zeros(5, 48, 64)
+    out = fusion.attention_fused(q, k, v, 0.1, torch.zeros(5, 40, 48, dtype=torch.bool))
+    assert seen == {"q": (1, 5, 40, 64), "k": (1, 5, 48, 64), "mask": (1, 5, 40, 48)}
+    assert tuple(out.shape) == (5, 40, 64)
+    q5 = torch.zeros(2, 3, 4, 40, 64)         # rank 5, 2-D mask kept
+    out = fusion.attention_fused(q5, torch.zeros(2, 3, 4, 48, 64), torch.zeros(2, 3, 4, 48, 64),
+                                 0.1, torch.zeros(40, 48, dtype=torch.bool))
+    assert seen["q"] == (1, 24, 40, 64) and seen["mask"] == (40, 48)
+    assert tuple(out.shape) == (2, 3, 4, 40, 64)
+    with pytest.raises(pkg_mod.VerifyError):
+        fusion.attention_fused(q, torch.zeros(4, 48, 64), torch.zeros(4, 48, 64), 0.1)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 2e-2), (torch.float32, 1e-4)])
 def test_fused_graph_matches_unfused_graph(pkg, fusion, dtype, tol):
@@ -171,3 +198,19 @@ def test_fused_graph_random_mask_and_keep_form(pkg, fusion):
     pkg.check_status(0)
     err = (out.float() - ref).abs().max().item() / ref.abs().max().item()
     assert np.isfinite(err) and err <= 2e-2
+
+
+@pytest.mark.gpu
+def test_fused_graph_rank3_operands(pkg, fusion):
+    """[H, N, D] operands (no batch dim) through the fused graph."""
+    g = torch.Generator(device="cuda").manual_seed(72)
+    H, N, D = 6, 256, 64
+    q, k, v = (torch.randn((H, N, D), generator=g, device="cuda").to(torch.bfloat16) for _ in range(3))
+    ref = unfused_div(q.float(), k.float(), v.float())
+    gm = torch.fx.symbolic_trace(unfused_div)
+    assert fusion.fuse_attention(gm) == 1
+    out = gm(q, k, v)
+    torch.cuda.synchronize()
+    pkg.check_status(0)
+    assert out.shape == (H, N, D)
+    assert (out.float() - ref).abs().max().item() / ref.abs().max().item() <= 2e-2
