@@ -437,11 +437,11 @@ def main():
     launches = pkg.launch_count() - n0
     clk = clocks.stop() if clocks else None
     pkg.check_status(local, stream)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.barrier()
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    from mlir_flashattention_b200.sharding import rank_values  # noqa: PLC0415
+    rank_ms = rank_values(ms, world, dev)  # each rank's timed region, in rank order
+    ms_max = max(rank_ms)
     ms_step = ms_max / args.steps
     job_flops = w.flops(slices) * world  # every rank holds the same shard size
     if args.scaling == "strong":
@@ -459,7 +459,8 @@ def main():
         validation = validate_gathered(w, q, k, v, out, rank, world, qd, kd, vd)
 
     if rank == 0:
-        emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validation, step_ms)
+        emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validation, step_ms,
+             rank_ms)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -589,8 +590,16 @@ def step_stats(step_ms):
             "over_5pct": bool(med > 0 and std / med > 0.05)}
 
 
+def rank_stats(rank_ms, steps):
+    """Per-step time of the slowest, median and fastest rank (ms); the
+    job's time is the slowest rank's."""
+    per = [m / steps for m in rank_ms]
+    return {"min": min(per), "median": statistics.median(per), "max": max(per),
+            "ranks": len(per)}
+
+
 def emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validation=None,
-         step_ms=None):
+         step_ms=None, rank_ms=None):
     peaks, peak_src = load_peaks()
     kernel_ms = ms / args.steps  # one launch per step on this rank
     achieved = w.flops(slices) / (kernel_ms * 1e-3) / 1e12
@@ -619,6 +628,8 @@ def emit(args, w, world, value, ms, ms_step, slices, launches, clk, e2e, validat
         "clocks": clk,
         "step_times": step_stats(step_ms),
     }
+    if rank_ms is not None and world > 1:
+        line["rank_ms_per_step"] = rank_stats(rank_ms, args.steps)
     if validation is not None:
         line["validation"] = validation
     if world == 1 and not args.no_cpu_baseline:

@@ -2,9 +2,10 @@
 
 Every (batch, head) slice of the attention op is an independent problem, so N
 processes (one per GPU) each own a contiguous block of slices and run with no
-collective on the data path.  The only collective is :func:`gather_rows`,
-used outside timed regions to bring sampled outputs to rank 0 for checking:
-NCCL over NVLink for CUDA tensors, gloo for CPU tensors.
+collective on the data path.  The collectives here run outside timed
+regions: :func:`gather_rows` brings sampled outputs to rank 0 for checking
+and :func:`rank_values` gathers each rank's timed duration (NCCL over NVLink
+for CUDA tensors, gloo for CPU tensors).
 
 For grouped-query attention a rank owns whole groups (all q-heads that share
 a kv head), so it needs only its own K/V heads.
@@ -40,3 +41,18 @@ def gather_rows(t, world: int, rank: int, dst: int = 0):
     if rank != dst:
         return None
     return [b[:s] for b, s in zip(bufs, sizes)]
+
+
+def rank_values(x: float, world: int, device=None):
+    """Every rank's value of ``x`` (a float), in rank order, on every rank.
+
+    Every rank must call it; with one rank no collective is made."""
+    if world == 1:
+        return [float(x)]
+    import torch  # noqa: PLC0415
+    import torch.distributed as dist  # noqa: PLC0415
+
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    return [float(v.item()) for v in parts]

@@ -41,6 +41,13 @@ def test_step_stats_median_spread_and_flag():
     assert abs(s["rel_std"] - s["std_ms"] / 2.12) < 1e-12 and s["over_5pct"] is True
 
 
+def test_rank_stats_slowest_rank_sets_the_time():
+    bench = _bench_module()
+    r = bench.rank_stats([20.0, 22.0, 21.0, 30.0], steps=10)
+    assert r["min"] == 2.0 and r["max"] == 3.0 and r["ranks"] == 4
+    assert abs(r["median"] - 2.15) < 1e-12
+
+
 def test_clock_record_reports_the_capped_part():
     """A timed region that starts at full clock and settles under the power
     cap: the record keeps the median, the minimum, the share of samples more

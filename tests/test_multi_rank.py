@@ -57,6 +57,15 @@ def _shard_worker(rank, world, port, out_path):
     dist.destroy_process_group()
 
 
+def _rank_values_worker(rank, world, port, out_path):
+    _, sharding, _ = _init(rank, world, port)
+    vals = sharding.rank_values(1.5 + rank, world)
+    if rank == 0:
+        np.save(out_path, np.array(vals))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def _early_exit_worker(rank, world, port, out_path):
     _, sharding, _ = _init(rank, world, port, timeout_s=5)
     if rank == 1:
@@ -75,6 +84,14 @@ def test_shards_gather_to_full_result(tmp_path):
     out = str(tmp_path / "err.npy")
     mp.spawn(_shard_worker, args=(2, _port(), out), nprocs=2, join=True)
     assert np.load(out)[0] == 0.0
+
+
+def test_rank_times_gathered_in_rank_order(tmp_path):
+    """The bench's max-over-ranks time: every rank's duration reaches every
+    rank, in rank order."""
+    out = str(tmp_path / "vals.npy")
+    mp.spawn(_rank_values_worker, args=(2, _port(), out), nprocs=2, join=True)
+    assert np.load(out).tolist() == [1.5, 2.5]
 
 
 def test_rank_leaving_early_is_detected(tmp_path):
