@@ -799,6 +799,47 @@ def test_negative_and_zero_scale(pkg, oracle, scale, kind, D):
     assert np.abs(L.cpu().numpy() - ref_lse).max() <= 1e-3
 
 
+@pytest.mark.parametrize("dtype,D,tol", [("bf16", 64, 2e-2), ("bf16", 128, 2e-2),
+                                         ("f32", 64, 1e-4)])
+@pytest.mark.parametrize("where", ["q", "k", "k_causal", "v"])
+def test_nan_inputs_propagate_like_the_reference(pkg, wl, oracle, dtype, D, tol, where):
+    """A NaN operand reaches exactly the outputs it reaches in the reference's
+    loop (arith.maximumf propagates NaN): a NaN in Q row r makes O row r and
+    its LSE NaN; a NaN key makes every row that sees it NaN (every row
+    without a mask; with the causal mask only rows at or after the key, the
+    mask select replacing the NaN score by -inf before it); a NaN in V
+    element (s, c) makes column c NaN in every row (0 x NaN included)."""
+    causal = where == "k_causal"
+    w = wl.Workload("t", dtype, 1, 2, 2, 384, D, causal, seed=61)
+    inp = wl.make_inputs(w)
+    if where == "q":
+        inp.q[0, 1, 5, 3] = np.nan
+    elif where in ("k", "k_causal"):
+        inp.k[0, 0, 300, 7] = np.nan
+    else:
+        inp.v[0, 1, 200, 9] = np.nan
+    for a, b in ((inp.qf, inp.q), (inp.kf, inp.k), (inp.vf, inp.v)):
+        assert a is b  # bf16 / f32 inputs: the oracle reads the same arrays
+    got, lse = _run_pkg(pkg, wl, w, inp, causal=causal)
+    ref, ref_lse = _ref(oracle, inp, w, causal)
+    nan = np.isnan(ref)
+    expect = np.zeros_like(nan)
+    if where == "q":
+        expect[0, 1, 5, :] = True
+    elif where == "k":
+        expect[0, 0] = True
+    elif where == "k_causal":
+        expect[0, 0, 300:] = True
+    else:
+        expect[0, 1, :, 9] = True
+    assert (nan == expect).all()
+    assert (np.isnan(got) == nan).all()
+    assert (np.isnan(lse) == np.isnan(ref_lse)).all()
+    assert _rel(got[~nan], ref[~nan]) <= tol
+    ok = ~np.isnan(ref_lse)
+    assert np.abs(lse[ok] - ref_lse[ok]).max() <= (1e-5 if dtype == "f32" else 1e-3)
+
+
 def test_concurrent_streams_match_serial(pkg, wl):
     """Calls on two streams at once (causal and dense-mask calls on one, a
     no-mask call on the other; the dense call's scratch is stream-ordered)
