@@ -70,13 +70,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking check of a phase: cheaper than a suspending try_wait when the
+// phase has usually completed already.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with parity `parity` of `bar` has completed.
 // Gives up after `limit_ns` of wall time or when *abort is raised; returns
 // false in that case (after recording kStatusTimeout on its own expiry).
+template <bool kProbeFirst = false>
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort, int* status,
                                                   uint64_t limit_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if constexpr (kProbeFirst) {
+    if (mbar_test_wait(bar, parity)) return true;
+  } else {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
   while (true) {
