@@ -25,8 +25,9 @@
 //               P·V_1(j).
 //   warps 0-3   softmax for Q tile 0, warps 4-7 for Q tile 1: one thread per
 //               query row reads its S row from TMEM, applies the mask, updates
-//               (m, l) in registers, writes P (bf16 / f16 / e4m3) back into the
-//               S columns (d = 64: P's own columns) and rescales its O row in
+//               (m, l) in registers, writes P (bf16 / f16) back into the S
+//               columns (d = 64: P's own columns; e4m3: a shared-memory
+//               tile) and rescales its O row in
 //               TMEM when m moved; at the end of a pair it writes O / l
 //               (through a shared-memory box per warp and a TMA tensor
 //               store) and the LSE.
