@@ -845,9 +845,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float mask_val = pos ? -INFINITY : INFINITY;
     int steps = 0;  // S tiles consumed so far (s_full / pv_done phases)
     bool ok = true;
-    // e4m3: the next work item, decoded ahead while the epilogue waits for
-    // the last P·V GEMM (c5 +2 %; the bf16 / f16 kernels' wait is shorter and
-    // measured slower with the extra work in front of it).
+    // e4m3 and d = 64 (no dense mask): the next work item, decoded ahead while
+    // the epilogue waits for the last P·V GEMM (c5 +2 %, bf16 d = 64 causal
+    // +3 %; the gated bf16 / f16 kernels' wait is shorter and measured slower
+    // with the extra work in front of it; the d = 64 dense kernels would spill).
+    constexpr bool kPreDecode = FP8 || (C::kEarlyS && !DENSE);
     int pre_rr = -1, pre_w = -1;
     Item pre_itm;
     for (int rr = 0; ok; ++rr) {
@@ -1090,7 +1092,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       // -------------------------------------------------------- epilogue
       // Work that does not read O, done while the last P·V GEMM completes:
-      // 1/l and (e4m3) the row's LSE and the next work item.  A split pair's
+      // 1/l and (kPreDecode) the row's LSE and the next work item.  A split pair's
       // halves merge their LSE below.
       const float inv_l = nan_row ? __int_as_float(0x7fc00000) : p.o_scale * vd / l;
       auto store_lse = [&]() {
@@ -1098,7 +1100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           p.lse[static_cast<int64_t>(itm.bh) * p.Nq + row] =
               nan_row ? __int_as_float(0x7fc00000) : (m + __log2f(l)) * 0.69314718055994531f;
       };
-      if constexpr (FP8) {
+      if constexpr (kPreDecode) {
         store_lse();
         pre_rr = rr + 1;
         pre_w = item_index<CAUSAL>(pre_rr, cta, G, W);
@@ -1271,7 +1273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if constexpr (!FP8) store_lse();
+      if constexpr (!kPreDecode) store_lse();
     }
   }
 
