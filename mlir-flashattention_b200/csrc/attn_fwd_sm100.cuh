@@ -95,6 +95,8 @@ struct FwdParams {
   int nkt;
   // Dense mode: work items (slice-major index) ordered by decreasing number
   // of KV tiles visited (order_dense_items), for the persistent schedule.
+  // Causal mode without a split: null, or a permutation of the work list
+  // that balances the snake's last rounds (planned by the host).
   const int* order;
   // Causal mode, KV split (split_pairs > 0): the split_pairs heaviest pair
   // indices of every slice run as two work items each, over the first and
@@ -490,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int r = 0; ok; ++r) {
           const int w = item_index<CAUSAL>(r, cta, G, W);
           if (w < 0) break;
-          const Item itm = decode_item<CAUSAL, SPLIT>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs, p.split_pairs);
+          const Item itm = decode_item<CAUSAL, SPLIT>((DENSE || p.order) ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs, p.split_pairs);
           const int b = itm.bh / p.Hq, h = itm.bh - (itm.bh / p.Hq) * p.Hq, hk = h / p.group;
           const PairSched<MODE, SPLIT> sc = make_sched<MODE, SPLIT>(itm, p);
           const int kt_end = sc.end();
@@ -608,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int r = 0; ok; ++r) {
         const int w = item_index<CAUSAL>(r, cta, G, W);
         if (w < 0) break;
-        const Item itm = decode_item<CAUSAL, SPLIT>(DENSE ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs, p.split_pairs);
+        const Item itm = decode_item<CAUSAL, SPLIT>((DENSE || p.order) ? __ldg(p.order + w) : w, p.num_bh, p.num_pairs, p.split_pairs);
         const PairSched<MODE, SPLIT> sc = make_sched<MODE, SPLIT>(itm, p);
         const int kt_end = sc.end();
         const int kt0 = sc.next(-1);
@@ -861,7 +863,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         w = item_index<CAUSAL>(rr, cta, G, W);
         if (w >= 0)
-          itm0 = decode_item<CAUSAL, SPLIT>(DENSE ? __ldg(p.order + w) : w, p.num_bh,
+          itm0 = decode_item<CAUSAL, SPLIT>((DENSE || p.order) ? __ldg(p.order + w) : w, p.num_bh,
                                              p.num_pairs, p.split_pairs);
       }
       if (w < 0) break;
@@ -1105,7 +1107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         pre_rr = rr + 1;
         pre_w = item_index<CAUSAL>(pre_rr, cta, G, W);
         if (pre_w >= 0)
-          pre_itm = decode_item<CAUSAL, SPLIT>(DENSE ? __ldg(p.order + pre_w) : pre_w, p.num_bh,
+          pre_itm = decode_item<CAUSAL, SPLIT>((DENSE || p.order) ? __ldg(p.order + pre_w) : pre_w, p.num_bh,
                                                p.num_pairs, p.split_pairs);
       }
       // The tile's last P·V GEMM has completed.
