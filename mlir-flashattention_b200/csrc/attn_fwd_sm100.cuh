@@ -411,6 +411,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   // there (e4m3 causal GQA +1 %, bf16 d = 64 causal +2-3 %); the gated
   // kernels' chain waits are mostly still pending and lose ~1.5 % with it.
   constexpr bool kProbe = C::kEarlyS;
+  // Gated bf16 / f16 kernels without a mask: P is published in two halves of
+  // 64 keys (p_ready[t], then p_ready[2 + t]) and the P·V GEMM is issued in
+  // two halves, the first while the softmax computes the second half of P
+  // (non-causal bf16 d = 128 +1.4 %; the causal kernel measured no gain).
+  constexpr bool kHalfP = !C::kEarlyS && !FP8 && MODE == kMaskNone;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -576,6 +581,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       // pbuf: the P buffer of this step (e4m3 P in shared memory).
+      auto issue_PV_half = [&](int t, int stage, bool acc, int half) {
+        const uint64_t b0 = dV0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
+        const uint32_t tP = tmem + t * 128;  // P_t's columns (its S columns)
+  #pragma unroll
+        for (int k = 0; k < C::kKStepsPV / 2; ++k) {
+          const int kk = half * (C::kKStepsPV / 2) + k;
+          mma_ts_lead<C::kKind>(lead, tmem + 256 + t * D, tP + kk * 8,
+                                b0 + static_cast<uint64_t>((kk * C::kKeysPerStep * 128) >> 4),
+                                idO, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
       auto issue_PV = [&](int t, int stage, bool acc, int pbuf) {
         const uint64_t b0 = dV0 + static_cast<uint64_t>((stage * C::kTileBytes) >> 4);
         if constexpr (C::kPSmem) {
@@ -773,7 +789,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = false;
                 break;
               }
-              ++p_cnt[t];
               // The first P·V GEMM of a pair overwrites O_t: the previous pair's
               // epilogue must have read it.
               if (first_pv[t] && items_t[t] > 0 && !wait(&o_free[t], items_t[t] - 1)) {
@@ -781,7 +796,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
               }
               tc_fence_after();
-              issue_PV(t, vst(i), !first_pv[t], 0);
+              if constexpr (kHalfP) {
+                // Keys 0-63 of P_t are stored: their half of the GEMM, then
+                // keys 64-127 once the softmax has stored them.
+                issue_PV_half(t, vst(i), !first_pv[t], 0);
+                if (!wait(&p_ready[2 + t], p_cnt[t])) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                issue_PV_half(t, vst(i), true, 1);
+              } else {
+                issue_PV(t, vst(i), !first_pv[t], 0);
+              }
+              ++p_cnt[t];
               first_pv[t] = false;
               mma_commit_lead(lead, &pv_done[t]);
               ++pv_cnt[t];
@@ -1008,6 +1036,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float neg_m = (m == -INFINITY) ? 0.f : -m;
         // x = s·sl2 − m and the row sums on packed fp32 pairs.
         const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(neg_m, neg_m);
+        if constexpr (kHalfP) {
+          // O_t rescaled first (the previous P·V GEMM has completed: its S GEMM
+          // followed it), then P in two halves, each published as it is stored.
+          const bool need_h = !first && (alpha != 1.f);
+          first = false;
+          if (__any_sync(0xffffffffu, need_h)) {
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(tO + c * 32, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st32(tO + c * 32, o);
+            }
+          }
+          uint64_t ha0 = f2_pack(0.f, 0.f), ha1 = ha0;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t pk[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const int cc = 32 * h + c;
+              float x0, x1;
+              f2_unpack(f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), sl2x2, negm2), x0, x1);
+              const float e0 = ex2(x0), e1 = ex2(x1);
+              const uint64_t pr = f2_pack(e0, e1);
+              if (c & 1) ha1 = f2_add(ha1, pr); else ha0 = f2_add(ha0, pr);
+              pk[c] = ELT == kEltF16 ? pack_f16(e0, e1) : pack_bf16(e0, e1);
+            }
+            tmem_st32(tP + 32 * h, pk);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(h == 0 ? &p_ready[t] : &p_ready[2 + t]);
+          }
+          float q0, q1;
+          f2_unpack(f2_add(ha0, ha1), q0, q1);
+          l = l * alpha + (q0 + q1);
+          kt = kn;
+          continue;
+        }
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           float x0, x1;
