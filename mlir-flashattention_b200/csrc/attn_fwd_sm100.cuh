@@ -18,7 +18,8 @@
 //               P·V_0(j), S_0(j'), P·V_1(j), S_1(j') where j' is the next
 //               KV tile of the pair's list (PairSched); each S GEMM is
 //               issued once the P·V GEMM reading P from its TMEM columns has
-//               completed (gate_S).
+//               completed (gate_S), and each P·V GEMM in two halves of 64
+//               keys as the softmax publishes the halves of P (kHalfP).
 //               d = 64 ("early S", P in columns of its own) and e4m3 (early
 //               S, P in shared memory, P·V in the SS form): S_0(j'), S_1(j')
 //               as soon as each softmax has read its S, then P·V_0(j),
