@@ -110,7 +110,10 @@ typedef struct AttnDesc {
  * Replaces the loop nest TilingPass.cpp:188-386 emits for one attention.fused.
  * Empty extents behave as that loop nest does: B, Hq or Nq = 0 computes
  * nothing (ATTN_OK); Nk = 0 runs no KV step, so every row of O is 0/0 = NaN
- * and the LSE is -inf. */
+ * and the LSE is -inf.  The first causal call of a shape with few work items
+ * per SM plans a balanced work order and keeps it in device memory (one
+ * cudaMalloc and a synchronous copy per device and shape, at most 64 shapes):
+ * make that first call outside stream capture. */
 ATTN_API int attn_fwd(const AttnDesc* desc, void* stream);
 
 /* Select and initialise `device` (idempotent): checks for sm_100, creates the
